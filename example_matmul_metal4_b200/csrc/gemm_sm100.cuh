@@ -1,0 +1,412 @@
+// Persistent warp-specialised GEMM for sm_100a: C = A * B (+ bias).
+//
+// Replaces the generated `matmul` kernel and the `reduce_sum_2` split-K
+// reduction of the reference (Sources/matmul/matmul.swift:239-296, :298-311).
+//
+// CTA = 6 warps, one CTA per SM, persistent over work units:
+//   warp 0     TMA producer: one elected lane streams A/B k-blocks (64 wide)
+//              into a STAGES-deep ring of 128-byte-swizzled smem tiles.
+//   warp 1     allocates TMEM; one elected lane issues tcgen05.mma
+//              (M=128, N=BN, K=16 per instruction) into one of two TMEM
+//              accumulators and commits each stage back to the producer.
+//   warps 2-5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//              32*(w%4)..+31, one output row per thread), add bias, round to
+//              fp16, store. With two accumulators the epilogue of one tile
+//              overlaps the main loop of the next.
+//
+// Split-K (MODE_SPLITK*): a work unit is (k-split, tile). Each unit adds its
+// fp32 partial into an L2-resident fp32 workspace with vector atomics, then
+// bumps a per-tile arrival counter; the unit that arrives last reads the
+// summed tile back, adds bias, writes the output and re-zeroes the workspace
+// and counter, so the workspace is clean for the next launch. The fp32
+// partials never round-trip through fp16 (the reference keeps fp16 partials,
+// matmul.swift:248, :298-311), and the K tail is applied exactly once (the
+// reference applies it in every split, matmul.swift:266-277).
+//
+// K tails need no special code: TMA zero-fills coordinates past K, so a
+// partial last k-block contributes zeros (replaces the dynamic_length_v op,
+// matmul.swift:271-277 and README.md:50-52).
+#pragma once
+
+#include "mm4_ptx.cuh"
+
+namespace mm4 {
+
+enum GemmMode : int {
+  MODE_DIRECT_F16 = 0,  // splits == 1: fp16 output + bias
+  MODE_SPLITK_F16 = 1,  // splits > 1: workspace reduce, fp16 output + bias
+  MODE_DIRECT_F32 = 2,  // splits == 1: fp32 output, no bias (K-shard partial)
+  MODE_SPLITK_F32 = 3,  // splits > 1: workspace reduce, fp32 output, no bias
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int num_m_tiles, num_n_tiles, num_tiles;
+  int splits, kb_total, num_units;
+  int group_m;            // raster: tiles are walked in groups of group_m M-tiles
+  const __half* bias;     // [N] or null
+  __half* C;              // [M][N] fp16 output (F16 modes)
+  float* C32;             // [M][N] fp32 output (F32 modes)
+  float* ws;              // [num_m_tiles*128][ws_ld] fp32, split-K only
+  int* counters;          // [num_tiles], split-K only
+  int ws_ld;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  // ring + barriers/slots + alignment slack
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+};
+
+// Wait-site ids recorded with MM4_ERR_TIMEOUT.
+enum : int {
+  SITE_GEMM_PRODUCER_EMPTY = 1,
+  SITE_GEMM_PRODUCER_DRAIN = 2,
+  SITE_GEMM_MMA_TMEM_EMPTY = 3,
+  SITE_GEMM_MMA_FULL = 4,
+  SITE_GEMM_MMA_DRAIN = 5,
+  SITE_GEMM_EPI_TMEM_FULL = 6,
+};
+
+struct GemmUnit {
+  int mt, nt, tile, kb0, kb1;
+};
+
+__device__ __forceinline__ GemmUnit gemm_decode_unit(const GemmArgs& a, int u) {
+  GemmUnit w;
+  int t, split;
+  if (a.splits > 1) {
+    // Units of one k-split are adjacent so co-resident CTAs share A/B k-slabs in L2.
+    split = u / a.num_tiles;
+    t = u - split * a.num_tiles;
+  } else {
+    split = 0;
+    t = u;
+  }
+  // Grouped raster: walk group_m M-tiles down a column of N-tiles.
+  const int group_size = a.group_m * a.num_n_tiles;
+  const int group = t / group_size;
+  const int first_m = group * a.group_m;
+  const int gm = min(a.num_m_tiles - first_m, a.group_m);
+  const int r = t - group * group_size;
+  w.mt = first_m + r % gm;
+  w.nt = r / gm;
+  w.tile = w.mt * a.num_n_tiles + w.nt;
+  w.kb0 = static_cast<int>((static_cast<long long>(split) * a.kb_total) / a.splits);
+  w.kb1 = static_cast<int>((static_cast<long long>(split + 1) * a.kb_total) / a.splits);
+  return w;
+}
+
+// All four epilogue warps agree on whether to proceed (every thread reaches
+// the two named barriers whatever its own wait returned, so none can hang).
+__device__ __forceinline__ bool epi_consensus(bool ok, int q, int lane, volatile int* s_vote) {
+  const int v = __all_sync(0xffffffffu, ok) ? 1 : 0;
+  if (lane == 0) s_vote[q] = v;
+  named_barrier(1, 128);
+  const bool all = (s_vote[0] & s_vote[1] & s_vote[2] & s_vote[3]) != 0;
+  named_barrier(1, 128);
+  return all;
+}
+
+template <int BN, bool A_MN, bool B_MN, int MODE>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
+  constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
+  constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* full = bars;                  // [STAGES]
+  uint64_t* empty = bars + STAGES;        // [STAGES]
+  uint64_t* tmem_full = bars + 2 * STAGES;   // [2]
+  uint64_t* tmem_empty = tmem_full + 2;      // [2]
+  uint64_t* drain = tmem_empty + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* s_vote = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [4]
+  volatile int* s_last = s_vote + 4;                                       // [1]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const Watchdog wd{args.status, args.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t fills = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
+        const GemmUnit w = gemm_decode_unit(args, u);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          const int s = static_cast<int>(fills % STAGES);
+          const uint32_t ph = (fills / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, wd, SITE_GEMM_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = ring + s * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          const int k0 = kb * GEMM_BK;
+          if (!A_MN) {
+            tma_load_2d(&tmA, &full[s], sA, k0, w.mt * GEMM_BM);
+          } else {
+            tma_load_2d(&tmA, &full[s], sA, w.mt * GEMM_BM, k0);
+            tma_load_2d(&tmA, &full[s], sA + 8192, w.mt * GEMM_BM + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(&tmB, &full[s], sB, k0, w.nt * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(&tmB, &full[s], sB + j * 8192, w.nt * BN + 64 * j, k0);
+          }
+          ++fills;
+        }
+      }
+      // Never leave with copies in flight: wait for the last fill of each stage.
+      const uint32_t first = fills > STAGES ? fills - STAGES : 0u;
+      for (uint32_t i = first; i < fills; ++i) {
+        if (!mbar_wait(&full[i % STAGES], (i / STAGES) & 1u, wd, SITE_GEMM_PRODUCER_DRAIN)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      uint32_t consumed = 0;
+      uint32_t tiles_done = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
+        const GemmUnit w = gemm_decode_unit(args, u);
+        const uint32_t acc = tiles_done & 1u;
+        const uint32_t aph = (tiles_done >> 1) & 1u;
+        if (!mbar_wait(&tmem_empty[acc], aph ^ 1u, wd, SITE_GEMM_MMA_TMEM_EMPTY)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          const int s = static_cast<int>(consumed % STAGES);
+          const uint32_t ph = (consumed / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, wd, SITE_GEMM_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ring + s * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            const uint64_t adesc =
+                A_MN ? sw128_desc(a_base + kk * 2048, 8192, 1024) : sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bdesc =
+                B_MN ? sw128_desc(b_base + kk * 2048, 8192, 1024) : sw128_desc(b_base + kk * 32, 16, 1024);
+            umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          ++consumed;
+        }
+        if (!ok) break;
+        umma_commit(&tmem_full[acc]);
+        ++tiles_done;
+      }
+      // All issued MMAs must finish before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, wd, SITE_GEMM_MMA_DRAIN);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    const int ethread = threadIdx.x - 64;  // 0..127
+    uint32_t tiles_done = 0;
+    for (int u = blockIdx.x; u < args.num_units; u += gridDim.x) {
+      const GemmUnit w = gemm_decode_unit(args, u);
+      const uint32_t acc = tiles_done & 1u;
+      const uint32_t aph = (tiles_done >> 1) & 1u;
+      bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
+      if (!epi_consensus(ok, q, lane, s_vote)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const int row = w.mt * GEMM_BM + row_in_tile;
+      const int col0 = w.nt * BN;
+
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[acc]);
+        }
+        const int cbase = col0 + c * 32;
+        if constexpr (SPLITK) {
+          float* dst = args.ws + static_cast<size_t>(row) * args.ws_ld + cbase;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            atomicAdd(reinterpret_cast<float4*>(dst + j),
+                      make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                  __uint_as_float(r[j + 3])));
+          }
+        } else if constexpr (OUT_F32) {
+          if (row < args.M) {
+            float* dst = args.C32 + static_cast<size_t>(row) * args.N + cbase;
+            const bool vec = (cbase + 32 <= args.N) && ((args.N & 3) == 0) &&
+                             ((reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0);
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (cbase + j < args.N) dst[j] = __uint_as_float(r[j]);
+            }
+          }
+        } else {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (args.bias != nullptr) {
+            if (cbase + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __half2float(args.bias[cbase + j]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (cbase + j < args.N) v[j] += __half2float(args.bias[cbase + j]);
+            }
+          }
+          if (row < args.M) {
+            __half* dst = args.C + static_cast<size_t>(row) * args.N + cbase;
+            const bool vec = (cbase + 32 <= args.N) && ((args.N & 7) == 0) &&
+                             ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
+            if (vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                pk.x = pack_half2(v[j], v[j + 1]);
+                pk.y = pack_half2(v[j + 2], v[j + 3]);
+                pk.z = pack_half2(v[j + 4], v[j + 5]);
+                pk.w = pack_half2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4*>(dst + j) = pk;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (cbase + j < args.N) dst[j] = __float2half_rn(v[j]);
+            }
+          }
+        }
+      }
+
+      if constexpr (SPLITK) {
+        // Publish this unit's partial, then count arrivals for the tile.
+        __threadfence();
+        named_barrier(1, 128);
+        if (ethread == 0) {
+          const int prev = atomicAdd(&args.counters[w.tile], 1);
+          *s_last = (prev == args.splits - 1) ? 1 : 0;
+        }
+        named_barrier(1, 128);
+        if (*s_last) {
+          __threadfence();
+          // Last arrival: finalize the whole tile, re-zero workspace + counter.
+          constexpr int TPR = BN / 4;          // threads per row (float4 each)
+          constexpr int RPI = 128 / TPR;       // rows per iteration
+          const int tr = ethread / TPR;
+          const int tc = (ethread % TPR) * 4;
+          const int gc = col0 + tc;
+          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+          if (!OUT_F32 && args.bias != nullptr) {
+            if (gc + 0 < args.N) b0 = __half2float(args.bias[gc + 0]);
+            if (gc + 1 < args.N) b1 = __half2float(args.bias[gc + 1]);
+            if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
+            if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
+          }
+#pragma unroll 4
+          for (int rr = tr; rr < GEMM_BM; rr += RPI) {
+            const int grow = w.mt * GEMM_BM + rr;
+            float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
+            const float4 s4 = __ldcg(src);
+            __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+            if (grow >= args.M) continue;
+            const float o0 = s4.x + b0, o1 = s4.y + b1, o2 = s4.z + b2, o3 = s4.w + b3;
+            if constexpr (OUT_F32) {
+              float* dst = args.C32 + static_cast<size_t>(grow) * args.N + gc;
+              if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0) {
+                *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
+              } else {
+                if (gc + 0 < args.N) dst[0] = o0;
+                if (gc + 1 < args.N) dst[1] = o1;
+                if (gc + 2 < args.N) dst[2] = o2;
+                if (gc + 3 < args.N) dst[3] = o3;
+              }
+            } else {
+              __half* dst = args.C + static_cast<size_t>(grow) * args.N + gc;
+              if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C) & 7u) == 0) {
+                uint2 pk;
+                pk.x = pack_half2(o0, o1);
+                pk.y = pack_half2(o2, o3);
+                *reinterpret_cast<uint2*>(dst) = pk;
+              } else {
+                if (gc + 0 < args.N) dst[0] = __float2half_rn(o0);
+                if (gc + 1 < args.N) dst[1] = __float2half_rn(o1);
+                if (gc + 2 < args.N) dst[2] = __float2half_rn(o2);
+                if (gc + 3 < args.N) dst[3] = __float2half_rn(o3);
+              }
+            }
+          }
+          if (ethread == 0) args.counters[w.tile] = 0;
+        }
+      }
+      ++tiles_done;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace mm4

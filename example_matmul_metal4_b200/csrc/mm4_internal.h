@@ -1,0 +1,50 @@
+// Host-side runtime shared by the mm4 translation units: error reporting,
+// per-device status words, device properties and TMA descriptor encoding.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "mm4.h"
+
+namespace mm4 {
+
+// Sets the thread-local message returned by mm4_last_error and returns `code`.
+mm4_status fail(mm4_status code, const char* fmt, ...);
+// Maps a CUDA error to MM4_ERR_CUDA with a message naming `what`.
+mm4_status cuda_fail(cudaError_t err, const char* what);
+
+#define MM4_CUDA_TRY(expr)                                  \
+  do {                                                      \
+    cudaError_t mm4_e_ = (expr);                            \
+    if (mm4_e_ != cudaSuccess) return ::mm4::cuda_fail(mm4_e_, #expr); \
+  } while (0)
+
+// Current device id, its SM count and whether it is an sm_100 part.
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t smem_optin = 0;
+};
+mm4_status current_device(DeviceInfo* info);
+
+// Device status word of the current device (lazily allocated, zeroed).
+mm4_status status_word(int** ptr);
+uint64_t wait_timeout_ns();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda, so the library loads on machines without a GPU).
+mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                        const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                        CUtensorMapSwizzle swizzle);
+
+// Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (kernel, device).
+mm4_status ensure_smem_attr(const void* kernel, int bytes);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace mm4

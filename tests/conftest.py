@@ -1,0 +1,24 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 GPU (runs on the B200 box)")
+    config.addinivalue_line("markers", "slow: long-running full-size case")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from example_matmul_metal4_b200 import lib
+    assert lib().mm4_device_supported() == 1, "libmm4 reports the device unsupported"
+    return torch.device("cuda:0")

@@ -1,0 +1,118 @@
+"""GEMM parity on the GPU: mm4 (through the C ABI) vs the C oracle
+(matmul.swift:499-510 restated), on seeded inputs."""
+import numpy as np
+import pytest
+
+import oracle
+from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan, MM4Error, lib, sync_check
+from example_matmul_metal4_b200 import data
+from example_matmul_metal4_b200.gemm import splitk_finalize
+from tolerance import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(M, N, K, tl, tr, seed, lo=-1.0, hi=1.0):
+    a_shape = (K, M) if tl else (M, K)
+    b_shape = (N, K) if tr else (K, N)
+    A = data.uniform(a_shape, lo, hi, seed, 0)
+    B = data.uniform(b_shape, lo, hi, seed, 1)
+    bias = data.uniform((N,), lo, hi, seed, 2)
+    return A, B, bias
+
+
+def _run(cuda, M, N, K, tl, tr, split=1, bias=True, seed=7, rows=None, dup=1):
+    import torch
+    A, B, b = _inputs(M, N, K, tl, tr, seed)
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(tl, tr), bias=bias, buildOptions=BuildOptions(splitK=split))
+    tA = torch.from_numpy(A).to(cuda)
+    tB = torch.from_numpy(B).to(cuda)
+    tb = torch.from_numpy(b).to(cuda)
+    C = plan.run(tA, tB, tb if bias else None, duplicatedCount=dup)
+    sync_check()
+    got = C.float().cpu().numpy()
+    ref = oracle.gemm(A, B, b if bias else None, M, N, K, tl, tr, rows=rows, threads=oracle.default_threads())
+    if rows:
+        got = got[rows[0]:rows[1]]
+    return plan, got, ref
+
+
+@pytest.mark.parametrize("tl,tr", [(False, False), (False, True), (True, False), (True, True)])
+def test_layouts(cuda, tl, tr):
+    plan, got, ref = _run(cuda, 256, 384, 320, tl, tr)
+    assert "sm100" in plan.kernel_name
+    assert_close(got, ref, f"layout tl={tl} tr={tr}")
+
+
+def test_baseline_config1_1024_nn_bias(cuda):
+    """M=N=K=1024, row-major NN, bias, U[-1,1], seed 1."""
+    plan, got, ref = _run(cuda, 1024, 1024, 1024, False, False, seed=1)
+    assert_close(got, ref, "1024^3")
+
+
+@pytest.mark.parametrize("M,N,K", [(200, 136, 200), (129, 264, 72), (1, 8, 8), (130, 520, 1000), (64, 64, 64)])
+def test_edges_and_k_tails(cuda, M, N, K):
+    plan, got, ref = _run(cuda, M, N, K, False, False)
+    assert "sm100" in plan.kernel_name
+    assert_close(got, ref, f"{M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("M,N,K", [(33, 40, 31), (17, 9, 1), (64, 33, 33)])
+def test_unaligned_uses_reduced_alignment_kernel(cuda, M, N, K):
+    plan, got, ref = _run(cuda, M, N, K, False, True)
+    assert "simt" in plan.kernel_name
+    assert_close(got, ref, f"{M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("K,split", [(8192, 32), (8192, 5), (4160, 7)])
+def test_split_k(cuda, K, split):
+    plan, got, ref = _run(cuda, 512, 512, K, False, False, split=split)
+    assert "splitk" in plan.kernel_name
+    assert_close(got, ref, f"split {split} K={K}")
+
+
+def test_split_k_repeat_leaves_workspace_clean(cuda):
+    """duplicatedCount re-runs the same launch; each run must re-zero its
+    workspace so every repetition produces the same result."""
+    plan, got, ref = _run(cuda, 256, 512, 4096, False, False, split=16, dup=3)
+    assert_close(got, ref, "split-K x3")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("K", [65536, 65520])
+def test_baseline_config2_split_k_full(cuda, K):
+    """M=N=512, K=65536 / 65520, split-K 32, seed 2."""
+    plan, got, ref = _run(cuda, 512, 512, K, False, False, split=32, seed=2)
+    assert_close(got, ref, f"512x512x{K}")
+
+
+def test_partial_and_finalize(cuda):
+    import torch
+    M, N, K = 256, 256, 1024
+    A, B, b = _inputs(M, N, K, False, False, 3)
+    tA, tB, tb = (torch.from_numpy(x).to(cuda) for x in (A, B, b))
+    # two K shards summed on the host side, then bias + cast
+    half = K // 2
+    p0 = GemmPlan(GEMMDimensions(M, N, half), transpose=(False, False), bias=False)
+    c0 = p0.partial(tA[:, :half].contiguous(), tB[:half].contiguous())
+    c1 = p0.partial(tA[:, half:].contiguous(), tB[half:].contiguous())
+    C = splitk_finalize(c0 + c1, tb)
+    sync_check()
+    ref = oracle.gemm(A, B, b, M, N, K, False, False, threads=oracle.default_threads())
+    assert_close(C.float().cpu().numpy(), ref, "partial+finalize")
+
+
+def test_bounded_wait_reports_timeout_and_context_survives(cuda):
+    L = lib()
+    assert L.mm4_debug_wait_timeout(2_000_000, None) == 0  # 2 ms
+    with pytest.raises(MM4Error) as e:
+        sync_check()
+    assert "TIMEOUT" in str(e.value)
+    # the context is still usable
+    plan, got, ref = _run(cuda, 128, 128, 128, False, False)
+    assert_close(got, ref, "after timeout")
+
+
+def test_invalid_descriptor_rejected():
+    with pytest.raises(MM4Error):
+        GemmPlan(GEMMDimensions(0, 16, 16))
