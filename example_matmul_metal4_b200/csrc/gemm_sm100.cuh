@@ -119,16 +119,220 @@ __device__ __forceinline__ bool epi_consensus(bool ok, int q, int lane, volatile
   return all;
 }
 
+
+// ---------------------------------------------------------------------------
+// MMA issuer role (one elected thread). Consumes `kb1 - kb0` ring stages per
+// work unit into one of two TMEM accumulators. PROXY_FENCE is set when the
+// ring is filled by ordinary (generic-proxy) stores instead of TMA.
+// ---------------------------------------------------------------------------
+template <int BN, bool A_MN, bool B_MN, int STAGES, int STAGE_BYTES, int A_BYTES, bool PROXY_FENCE>
+__device__ __forceinline__ void mma_role(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                         uint64_t* tmem_full, uint64_t* tmem_empty, uint64_t* drain,
+                                         uint32_t tmem_base, const Watchdog& wd) {
+  constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BM, BN, A_MN, B_MN);
+  uint32_t consumed = 0;
+  uint32_t tiles_done = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
+    const GemmUnit w = gemm_decode_unit(args, u);
+    const uint32_t acc = tiles_done & 1u;
+    const uint32_t aph = (tiles_done >> 1) & 1u;
+    if (!mbar_wait(&tmem_empty[acc], aph ^ 1u, wd, SITE_GEMM_MMA_TMEM_EMPTY)) break;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + acc * BN;
+    for (int kb = w.kb0; kb < w.kb1; ++kb) {
+      const int s = static_cast<int>(consumed % STAGES);
+      const uint32_t ph = (consumed / STAGES) & 1u;
+      if (!mbar_wait(&full[s], ph, wd, SITE_GEMM_MMA_FULL)) {
+        ok = false;
+        break;
+      }
+      if (PROXY_FENCE) fence_proxy_async_smem();
+      tc_fence_after();
+      const uint32_t a_base = smem_u32(ring + s * STAGE_BYTES);
+      const uint32_t b_base = a_base + A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+        const uint64_t adesc =
+            A_MN ? sw128_desc(a_base + kk * 2048, 8192, 1024) : sw128_desc(a_base + kk * 32, 16, 1024);
+        const uint64_t bdesc =
+            B_MN ? sw128_desc(b_base + kk * 2048, 8192, 1024) : sw128_desc(b_base + kk * 32, 16, 1024);
+        umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+      ++consumed;
+    }
+    if (!ok) break;
+    umma_commit(&tmem_full[acc]);
+    ++tiles_done;
+  }
+  // All issued MMAs must finish before TMEM is released.
+  umma_commit(drain);
+  mbar_wait(drain, 0, wd, SITE_GEMM_MMA_DRAIN);
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue role (warps 2-5 of the CTA, 128 threads: thread 64 + i).
+// ---------------------------------------------------------------------------
+template <int BN, int MODE>
+__device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tmem_full, uint64_t* tmem_empty,
+                                              uint32_t tmem_base, volatile int* s_vote, volatile int* s_last,
+                                              const Watchdog& wd, int warp, int lane) {
+  constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
+  constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
+  const int q = warp & 3;  // TMEM lane quarter this warp may access
+  const int row_in_tile = q * 32 + lane;
+  const int ethread = threadIdx.x - 64;  // 0..127
+  uint32_t tiles_done = 0;
+  for (int u = blockIdx.x; u < args.num_units; u += gridDim.x) {
+    const GemmUnit w = gemm_decode_unit(args, u);
+    const uint32_t acc = tiles_done & 1u;
+    const uint32_t aph = (tiles_done >> 1) & 1u;
+    bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
+    if (!epi_consensus(ok, q, lane, s_vote)) break;
+    tc_fence_after();
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+    const int row = w.mt * GEMM_BM + row_in_tile;
+    const int col0 = w.nt * BN;
+
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + c * 32, r);
+      tmem_ld_wait();
+      if (c == BN / 32 - 1) {
+        tc_fence_before();
+        mbar_arrive(&tmem_empty[acc]);
+      }
+      const int cbase = col0 + c * 32;
+      if constexpr (SPLITK) {
+        float* dst = args.ws + static_cast<size_t>(row) * args.ws_ld + cbase;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          atomicAdd(reinterpret_cast<float4*>(dst + j),
+                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                __uint_as_float(r[j + 3])));
+        }
+      } else if constexpr (OUT_F32) {
+        if (row < args.M) {
+          float* dst = args.C32 + static_cast<size_t>(row) * args.N + cbase;
+          const bool vec = (cbase + 32 <= args.N) && ((args.N & 3) == 0) &&
+                           ((reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (cbase + j < args.N) dst[j] = __uint_as_float(r[j]);
+          }
+        }
+      } else {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (args.bias != nullptr) {
+          if (cbase + 32 <= args.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += __half2float(args.bias[cbase + j]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (cbase + j < args.N) v[j] += __half2float(args.bias[cbase + j]);
+          }
+        }
+        if (row < args.M) {
+          __half* dst = args.C + static_cast<size_t>(row) * args.N + cbase;
+          const bool vec = (cbase + 32 <= args.N) && ((args.N & 7) == 0) &&
+                           ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 pk;
+              pk.x = pack_half2(v[j], v[j + 1]);
+              pk.y = pack_half2(v[j + 2], v[j + 3]);
+              pk.z = pack_half2(v[j + 4], v[j + 5]);
+              pk.w = pack_half2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(dst + j) = pk;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (cbase + j < args.N) dst[j] = __float2half_rn(v[j]);
+          }
+        }
+      }
+    }
+
+    if constexpr (SPLITK) {
+      // Publish this unit's partial, then count arrivals for the tile.
+      __threadfence();
+      named_barrier(1, 128);
+      if (ethread == 0) {
+        const int prev = atomicAdd(&args.counters[w.tile], 1);
+        *s_last = (prev == args.splits - 1) ? 1 : 0;
+      }
+      named_barrier(1, 128);
+      if (*s_last) {
+        __threadfence();
+        // Last arrival: finalize the whole tile, re-zero workspace + counter.
+        constexpr int TPR = BN / 4;          // threads per row (float4 each)
+        constexpr int RPI = 128 / TPR;       // rows per iteration
+        const int tr = ethread / TPR;
+        const int tc = (ethread % TPR) * 4;
+        const int gc = col0 + tc;
+        float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+        if (!OUT_F32 && args.bias != nullptr) {
+          if (gc + 0 < args.N) b0 = __half2float(args.bias[gc + 0]);
+          if (gc + 1 < args.N) b1 = __half2float(args.bias[gc + 1]);
+          if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
+          if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
+        }
+#pragma unroll 4
+        for (int rr = tr; rr < GEMM_BM; rr += RPI) {
+          const int grow = w.mt * GEMM_BM + rr;
+          float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
+          const float4 s4 = __ldcg(src);
+          __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+          if (grow >= args.M) continue;
+          const float o0 = s4.x + b0, o1 = s4.y + b1, o2 = s4.z + b2, o3 = s4.w + b3;
+          if constexpr (OUT_F32) {
+            float* dst = args.C32 + static_cast<size_t>(grow) * args.N + gc;
+            if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0) {
+              *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
+            } else {
+              if (gc + 0 < args.N) dst[0] = o0;
+              if (gc + 1 < args.N) dst[1] = o1;
+              if (gc + 2 < args.N) dst[2] = o2;
+              if (gc + 3 < args.N) dst[3] = o3;
+            }
+          } else {
+            __half* dst = args.C + static_cast<size_t>(grow) * args.N + gc;
+            if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C) & 7u) == 0) {
+              uint2 pk;
+              pk.x = pack_half2(o0, o1);
+              pk.y = pack_half2(o2, o3);
+              *reinterpret_cast<uint2*>(dst) = pk;
+            } else {
+              if (gc + 0 < args.N) dst[0] = __float2half_rn(o0);
+              if (gc + 1 < args.N) dst[1] = __float2half_rn(o1);
+              if (gc + 2 < args.N) dst[2] = __float2half_rn(o2);
+              if (gc + 3 < args.N) dst[3] = __float2half_rn(o3);
+            }
+          }
+        }
+        if (ethread == 0) args.counters[w.tile] = 0;
+      }
+    }
+    ++tiles_done;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
-  constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
-  constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BM, BN, A_MN, B_MN);
-
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -211,194 +415,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      uint32_t consumed = 0;
-      uint32_t tiles_done = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
-        const GemmUnit w = gemm_decode_unit(args, u);
-        const uint32_t acc = tiles_done & 1u;
-        const uint32_t aph = (tiles_done >> 1) & 1u;
-        if (!mbar_wait(&tmem_empty[acc], aph ^ 1u, wd, SITE_GEMM_MMA_TMEM_EMPTY)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          const int s = static_cast<int>(consumed % STAGES);
-          const uint32_t ph = (consumed / STAGES) & 1u;
-          if (!mbar_wait(&full[s], ph, wd, SITE_GEMM_MMA_FULL)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(ring + s * Cfg::STAGE_BYTES);
-          const uint32_t b_base = a_base + Cfg::A_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-            const uint64_t adesc =
-                A_MN ? sw128_desc(a_base + kk * 2048, 8192, 1024) : sw128_desc(a_base + kk * 32, 16, 1024);
-            const uint64_t bdesc =
-                B_MN ? sw128_desc(b_base + kk * 2048, 8192, 1024) : sw128_desc(b_base + kk * 32, 16, 1024);
-            umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&empty[s]);
-          ++consumed;
-        }
-        if (!ok) break;
-        umma_commit(&tmem_full[acc]);
-        ++tiles_done;
-      }
-      // All issued MMAs must finish before TMEM is released.
-      umma_commit(drain);
-      mbar_wait(drain, 0, wd, SITE_GEMM_MMA_DRAIN);
-    }
+    if (elect_one())
+      mma_role<BN, A_MN, B_MN, STAGES, Cfg::STAGE_BYTES, Cfg::A_BYTES, false>(args, ring, full, empty, tmem_full,
+                                                                           tmem_empty, drain, tmem_base, wd);
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = q * 32 + lane;
-    const int ethread = threadIdx.x - 64;  // 0..127
-    uint32_t tiles_done = 0;
-    for (int u = blockIdx.x; u < args.num_units; u += gridDim.x) {
-      const GemmUnit w = gemm_decode_unit(args, u);
-      const uint32_t acc = tiles_done & 1u;
-      const uint32_t aph = (tiles_done >> 1) & 1u;
-      bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
-      if (!epi_consensus(ok, q, lane, s_vote)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      const int row = w.mt * GEMM_BM + row_in_tile;
-      const int col0 = w.nt * BN;
-
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_ld_wait();
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&tmem_empty[acc]);
-        }
-        const int cbase = col0 + c * 32;
-        if constexpr (SPLITK) {
-          float* dst = args.ws + static_cast<size_t>(row) * args.ws_ld + cbase;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            atomicAdd(reinterpret_cast<float4*>(dst + j),
-                      make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                  __uint_as_float(r[j + 3])));
-          }
-        } else if constexpr (OUT_F32) {
-          if (row < args.M) {
-            float* dst = args.C32 + static_cast<size_t>(row) * args.N + cbase;
-            const bool vec = (cbase + 32 <= args.N) && ((args.N & 3) == 0) &&
-                             ((reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0);
-            if (vec) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < args.N) dst[j] = __uint_as_float(r[j]);
-            }
-          }
-        } else {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if (args.bias != nullptr) {
-            if (cbase + 32 <= args.N) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += __half2float(args.bias[cbase + j]);
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < args.N) v[j] += __half2float(args.bias[cbase + j]);
-            }
-          }
-          if (row < args.M) {
-            __half* dst = args.C + static_cast<size_t>(row) * args.N + cbase;
-            const bool vec = (cbase + 32 <= args.N) && ((args.N & 7) == 0) &&
-                             ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
-            if (vec) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                pk.x = pack_half2(v[j], v[j + 1]);
-                pk.y = pack_half2(v[j + 2], v[j + 3]);
-                pk.z = pack_half2(v[j + 4], v[j + 5]);
-                pk.w = pack_half2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(dst + j) = pk;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < args.N) dst[j] = __float2half_rn(v[j]);
-            }
-          }
-        }
-      }
-
-      if constexpr (SPLITK) {
-        // Publish this unit's partial, then count arrivals for the tile.
-        __threadfence();
-        named_barrier(1, 128);
-        if (ethread == 0) {
-          const int prev = atomicAdd(&args.counters[w.tile], 1);
-          *s_last = (prev == args.splits - 1) ? 1 : 0;
-        }
-        named_barrier(1, 128);
-        if (*s_last) {
-          __threadfence();
-          // Last arrival: finalize the whole tile, re-zero workspace + counter.
-          constexpr int TPR = BN / 4;          // threads per row (float4 each)
-          constexpr int RPI = 128 / TPR;       // rows per iteration
-          const int tr = ethread / TPR;
-          const int tc = (ethread % TPR) * 4;
-          const int gc = col0 + tc;
-          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-          if (!OUT_F32 && args.bias != nullptr) {
-            if (gc + 0 < args.N) b0 = __half2float(args.bias[gc + 0]);
-            if (gc + 1 < args.N) b1 = __half2float(args.bias[gc + 1]);
-            if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
-            if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
-          }
-#pragma unroll 4
-          for (int rr = tr; rr < GEMM_BM; rr += RPI) {
-            const int grow = w.mt * GEMM_BM + rr;
-            float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
-            const float4 s4 = __ldcg(src);
-            __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
-            if (grow >= args.M) continue;
-            const float o0 = s4.x + b0, o1 = s4.y + b1, o2 = s4.z + b2, o3 = s4.w + b3;
-            if constexpr (OUT_F32) {
-              float* dst = args.C32 + static_cast<size_t>(grow) * args.N + gc;
-              if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0) {
-                *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
-              } else {
-                if (gc + 0 < args.N) dst[0] = o0;
-                if (gc + 1 < args.N) dst[1] = o1;
-                if (gc + 2 < args.N) dst[2] = o2;
-                if (gc + 3 < args.N) dst[3] = o3;
-              }
-            } else {
-              __half* dst = args.C + static_cast<size_t>(grow) * args.N + gc;
-              if (gc + 4 <= args.N && (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(args.C) & 7u) == 0) {
-                uint2 pk;
-                pk.x = pack_half2(o0, o1);
-                pk.y = pack_half2(o2, o3);
-                *reinterpret_cast<uint2*>(dst) = pk;
-              } else {
-                if (gc + 0 < args.N) dst[0] = __float2half_rn(o0);
-                if (gc + 1 < args.N) dst[1] = __float2half_rn(o1);
-                if (gc + 2 < args.N) dst[2] = __float2half_rn(o2);
-                if (gc + 3 < args.N) dst[3] = __float2half_rn(o3);
-              }
-            }
-          }
-          if (ethread == 0) args.counters[w.tile] = 0;
-        }
-      }
-      ++tiles_done;
-    }
+    epilogue_role<BN, MODE>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, wd, warp, lane);
   }
 
   tc_fence_before();

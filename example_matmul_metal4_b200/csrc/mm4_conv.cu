@@ -1,0 +1,276 @@
+// Convolution plans and dispatch (conv2d / conv3d as one implicit-GEMM
+// launch) and the weight-layout permutation.
+//
+// Replaces TensorOpSession / TensorOpSession3D / TensorOpBiasSession3D /
+// TensorOpHorizontalPaddingSession3D / WeightPermutationSession3D
+// (ConvolutionShared.swift:844-1675) and the padded conv2d probe session
+// (convolution2d_padding.swift:235-290).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "conv_sm100.cuh"
+#include "mm4_internal.h"
+
+using namespace mm4;
+
+struct mm4_conv_plan {
+  ConvGeom g;  // pointers filled per run
+  int bias;
+  int bn;
+  long long m_total;
+  int num_m_tiles, num_n_tiles;
+  bool w_tma_shape;  // weight pitch allows TMA (pointer alignment checked per run)
+  bool w_mn;         // HWIO / DHWIO: Cout contiguous
+  char name[96];
+};
+
+namespace {
+
+int out_size(int in, int plo, int phi, int k, int s, int d) { return (in + plo + phi - ((k - 1) * d + 1)) / s + 1; }
+
+mm4_status finish_plan(mm4_conv_plan* p) {
+  ConvGeom& g = p->g;
+  if (g.OD <= 0 || g.OH <= 0 || g.OW <= 0)
+    return fail(MM4_ERR_INVALID, "convolution output is empty (OD=%d OH=%d OW=%d)", g.OD, g.OH, g.OW);
+  g.ncb = (g.C + 63) / 64;
+  g.taps = g.KD * g.KH * g.KW;
+  p->m_total = static_cast<long long>(g.N) * g.OD * g.OH * g.OW;
+  if (p->m_total > (1ll << 31) - 256) return fail(MM4_ERR_UNSUPPORTED, "too many output pixels");
+  p->bn = g.O <= 128 ? 128 : 256;
+  p->num_m_tiles = static_cast<int>((p->m_total + GEMM_BM - 1) / GEMM_BM);
+  p->num_n_tiles = (g.O + p->bn - 1) / p->bn;
+  p->w_mn = (g.w_layout == MM4_WEIGHTS_HWIO || g.w_layout == MM4_WEIGHTS_DHWIO);
+  p->w_tma_shape = p->w_mn ? (g.O % 8 == 0) : (g.C % 8 == 0);
+  snprintf(p->name, sizeof(p->name), "conv_sm100<BN=%d,%s,%s>", p->bn,
+           p->w_tma_shape ? (p->w_mn ? "W:tma-MN" : "W:tma-K") : "W:gather",
+           (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
+  return MM4_OK;
+}
+
+template <int BN, bool B_TMA, bool B_MN>
+mm4_status launch(const CUtensorMap& tm, const GemmArgs& args, const ConvGeom& g, int grid, cudaStream_t st) {
+  auto kern = conv_sm100_kernel<BN, B_TMA, B_MN>;
+  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+  mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
+  if (rc != MM4_OK) return rc;
+  kern<<<grid, CONV_THREADS, smem, st>>>(tm, args, g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "conv_sm100_kernel launch");
+  return MM4_OK;
+}
+
+template <int BN>
+mm4_status launch_bn(bool tma, bool mn, const CUtensorMap& tm, const GemmArgs& args, const ConvGeom& g, int grid,
+                     cudaStream_t st) {
+  if (!tma) return launch<BN, false, false>(tm, args, g, grid, st);
+  if (mn) return launch<BN, true, true>(tm, args, g, grid, st);
+  return launch<BN, true, false>(tm, args, g, grid, st);
+}
+
+mm4_status check_layout_2d(int layout) {
+  if (layout != MM4_WEIGHTS_HWIO && layout != MM4_WEIGHTS_OHWI)
+    return fail(MM4_ERR_INVALID, "conv2d weight_layout must be MM4_WEIGHTS_HWIO or MM4_WEIGHTS_OHWI (got %d)", layout);
+  return MM4_OK;
+}
+
+mm4_status check_layout_3d(int layout) {
+  if (layout != MM4_WEIGHTS_DHWIO && layout != MM4_WEIGHTS_ODHWI)
+    return fail(MM4_ERR_INVALID, "conv3d weight_layout must be MM4_WEIGHTS_DHWIO or MM4_WEIGHTS_ODHWI (got %d)",
+                layout);
+  return MM4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mm4_status mm4_conv2d_plan_create(mm4_conv_plan** out, const mm4_conv2d_desc* d) {
+  if (!out) return fail(MM4_ERR_INVALID, "null plan pointer");
+  *out = nullptr;
+  if (!d) return fail(MM4_ERR_INVALID, "null conv2d descriptor");
+  if (d->batch_size <= 0 || d->input_height <= 0 || d->input_width <= 0 || d->input_channels <= 0 ||
+      d->output_channels <= 0 || d->kernel_height <= 0 || d->kernel_width <= 0 || d->stride_y <= 0 ||
+      d->stride_x <= 0 || d->dilation_y <= 0 || d->dilation_x <= 0 || d->padding_top < 0 || d->padding_bottom < 0 ||
+      d->padding_left < 0 || d->padding_right < 0)
+    return fail(MM4_ERR_INVALID, "conv2d dimensions must be positive and paddings non-negative");
+  mm4_status rc = check_layout_2d(d->weight_layout);
+  if (rc != MM4_OK) return rc;
+  mm4_conv_plan* p = new (std::nothrow) mm4_conv_plan();
+  if (!p) return fail(MM4_ERR_INVALID, "out of host memory");
+  ConvGeom& g = p->g;
+  g.N = d->batch_size;
+  g.D = 1;
+  g.H = d->input_height;
+  g.W = d->input_width;
+  g.C = d->input_channels;
+  g.O = d->output_channels;
+  g.KD = 1;
+  g.KH = d->kernel_height;
+  g.KW = d->kernel_width;
+  g.SZ = 1;
+  g.SY = d->stride_y;
+  g.SX = d->stride_x;
+  g.DZ = 1;
+  g.DY = d->dilation_y;
+  g.DX = d->dilation_x;
+  g.PF = 0;
+  g.PT = d->padding_top;
+  g.PL = d->padding_left;
+  g.OD = 1;
+  g.OH = out_size(g.H, d->padding_top, d->padding_bottom, g.KH, g.SY, g.DY);
+  g.OW = out_size(g.W, d->padding_left, d->padding_right, g.KW, g.SX, g.DX);
+  g.w_layout = d->weight_layout;
+  p->bias = d->bias ? 1 : 0;
+  rc = finish_plan(p);
+  if (rc != MM4_OK) {
+    delete p;
+    return rc;
+  }
+  *out = p;
+  return MM4_OK;
+}
+
+mm4_status mm4_conv3d_plan_create(mm4_conv_plan** out, const mm4_conv3d_desc* d) {
+  if (!out) return fail(MM4_ERR_INVALID, "null plan pointer");
+  *out = nullptr;
+  if (!d) return fail(MM4_ERR_INVALID, "null conv3d descriptor");
+  if (d->batch_size <= 0 || d->input_depth <= 0 || d->input_height <= 0 || d->input_width <= 0 ||
+      d->input_channels <= 0 || d->output_channels <= 0 || d->kernel_depth <= 0 || d->kernel_height <= 0 ||
+      d->kernel_width <= 0 || d->stride_z <= 0 || d->stride_y <= 0 || d->stride_x <= 0 || d->dilation_z <= 0 ||
+      d->dilation_y <= 0 || d->dilation_x <= 0 || d->padding_top < 0 || d->padding_bottom < 0 ||
+      d->padding_left < 0 || d->padding_right < 0 || d->padding_front < 0 || d->padding_back < 0)
+    return fail(MM4_ERR_INVALID, "conv3d dimensions must be positive and paddings non-negative");
+  mm4_status rc = check_layout_3d(d->weight_layout);
+  if (rc != MM4_OK) return rc;
+  mm4_conv_plan* p = new (std::nothrow) mm4_conv_plan();
+  if (!p) return fail(MM4_ERR_INVALID, "out of host memory");
+  ConvGeom& g = p->g;
+  g.N = d->batch_size;
+  g.D = d->input_depth;
+  g.H = d->input_height;
+  g.W = d->input_width;
+  g.C = d->input_channels;
+  g.O = d->output_channels;
+  g.KD = d->kernel_depth;
+  g.KH = d->kernel_height;
+  g.KW = d->kernel_width;
+  g.SZ = d->stride_z;
+  g.SY = d->stride_y;
+  g.SX = d->stride_x;
+  g.DZ = d->dilation_z;
+  g.DY = d->dilation_y;
+  g.DX = d->dilation_x;
+  g.PF = d->padding_front;
+  g.PT = d->padding_top;
+  g.PL = d->padding_left;
+  g.OD = out_size(g.D, d->padding_front, d->padding_back, g.KD, g.SZ, g.DZ);
+  g.OH = out_size(g.H, d->padding_top, d->padding_bottom, g.KH, g.SY, g.DY);
+  g.OW = out_size(g.W, d->padding_left, d->padding_right, g.KW, g.SX, g.DX);
+  g.w_layout = d->weight_layout;
+  p->bias = d->bias ? 1 : 0;
+  rc = finish_plan(p);
+  if (rc != MM4_OK) {
+    delete p;
+    return rc;
+  }
+  *out = p;
+  return MM4_OK;
+}
+
+void mm4_conv_plan_destroy(mm4_conv_plan* plan) { delete plan; }
+
+const char* mm4_conv_plan_kernel_name(const mm4_conv_plan* plan) { return plan ? plan->name : ""; }
+
+int64_t mm4_conv_output_elements(const mm4_conv_plan* plan) {
+  return plan ? plan->m_total * plan->g.O : 0;
+}
+
+mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, const void* bias, void* y,
+                        mm4_stream_t stream, int duplicated_count) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!x || !w || !y) return fail(MM4_ERR_INVALID, "null x/w/y pointer");
+  if (p->bias && !bias) return fail(MM4_ERR_INVALID, "plan has bias but bias pointer is null");
+  if (duplicated_count < 1) return fail(MM4_ERR_INVALID, "duplicated_count must be >= 1");
+  DeviceInfo info;
+  mm4_status rc = current_device(&info);
+  if (rc != MM4_OK) return rc;
+  int* status = nullptr;
+  rc = status_word(&status);
+  if (rc != MM4_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  ConvGeom g = p->g;
+  g.x = static_cast<const __half*>(x);
+  g.w = static_cast<const __half*>(w);
+  g.x_vec = (g.C % 8 == 0) && aligned16(x);
+  const bool tma = p->w_tma_shape && aligned16(w);
+
+  CUtensorMap tm;
+  memset(&tm, 0, sizeof(tm));
+  if (tma) {
+    if (!p->w_mn) {  // [Cout][taps][Cin]
+      const uint64_t dims[3] = {static_cast<uint64_t>(g.C), static_cast<uint64_t>(g.taps),
+                                static_cast<uint64_t>(g.O)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(g.C) * 2, static_cast<uint64_t>(g.taps) * g.C * 2};
+      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(p->bn)};
+      rc = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {  // [taps][Cin][Cout]
+      const uint64_t dims[3] = {static_cast<uint64_t>(g.O), static_cast<uint64_t>(g.C),
+                                static_cast<uint64_t>(g.taps)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(g.O) * 2, static_cast<uint64_t>(g.C) * g.O * 2};
+      const uint32_t box[3] = {64, 64, 1};
+      rc = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc != MM4_OK) return rc;
+  }
+
+  GemmArgs args{};
+  args.M = static_cast<int>(p->m_total);
+  args.N = g.O;
+  args.K = g.taps * g.C;
+  args.num_m_tiles = p->num_m_tiles;
+  args.num_n_tiles = p->num_n_tiles;
+  args.num_tiles = p->num_m_tiles * p->num_n_tiles;
+  args.splits = 1;
+  args.kb_total = g.taps * g.ncb;
+  args.num_units = args.num_tiles;
+  args.group_m = 16;
+  args.bias = p->bias ? static_cast<const __half*>(bias) : nullptr;
+  args.C = static_cast<__half*>(y);
+  args.status = status;
+  args.timeout_ns = wait_timeout_ns();
+  const int grid = std::min(args.num_units, info.sm_count);
+  for (int i = 0; i < duplicated_count; ++i) {
+    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, tm, args, g, grid, st)
+                        : launch_bn<128>(tma, p->w_mn, tm, args, g, grid, st);
+    if (rc != MM4_OK) return rc;
+  }
+  return MM4_OK;
+}
+
+mm4_status mm4_permute_weights(int from, int to, const int32_t dims[5], const void* src, void* dst,
+                               mm4_stream_t stream) {
+  if (!dims || !src || !dst) return fail(MM4_ERR_INVALID, "null argument");
+  const bool from2 = from >= 0 && from <= 2, to2 = to >= 0 && to <= 2;
+  const bool from3 = from >= 3 && from <= 5, to3 = to >= 3 && to <= 5;
+  if (!((from2 && to2) || (from3 && to3)))
+    return fail(MM4_ERR_INVALID, "permute needs two 2-D or two 3-D weight layouts (got %d -> %d)", from, to);
+  const int O = dims[0], C = dims[1], KD = dims[2], KH = dims[3], KW = dims[4];
+  if (O <= 0 || C <= 0 || KD <= 0 || KH <= 0 || KW <= 0) return fail(MM4_ERR_INVALID, "dims must be positive");
+  if (from2 && KD != 1) return fail(MM4_ERR_INVALID, "2-D layouts need KD == 1");
+  if (src == dst) return fail(MM4_ERR_INVALID, "permute cannot run in place");
+  DeviceInfo info;
+  mm4_status rc = current_device(&info);
+  if (rc != MM4_OK) return rc;
+  const long long total = static_cast<long long>(O) * C * KD * KH * KW;
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, static_cast<long long>(info.sm_count) * 16));
+  permute_weights_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      from, to, O, C, KD, KH, KW, static_cast<const unsigned short*>(src), static_cast<unsigned short*>(dst));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "permute_weights_kernel launch");
+  return MM4_OK;
+}
+
+}  // extern "C"
