@@ -82,6 +82,7 @@ SIGNATURES = {
     "mm4_gemm_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, ctypes.c_int]),
     "mm4_gemm_partial_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mm4_splitk_finalize": (ctypes.c_int, [_i32, _i32, _vp, _vp, _vp, _vp]),
+    "mm4_gemm_splitk_run_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "mm4_attention_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(AttentionDesc)]),
     "mm4_attention_plan_destroy": (None, [_vp]),
     "mm4_attention_plan_kernel_name": (ctypes.c_char_p, [_vp]),

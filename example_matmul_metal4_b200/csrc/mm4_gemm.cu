@@ -11,21 +11,11 @@
 
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
+#include "mm4_gemm_plan.h"
 #include "mm4_internal.h"
 
 using namespace mm4;
 
-struct mm4_gemm_plan {
-  mm4_gemm_desc d;
-  bool tensor_core;  // false: reduced-alignment SIMT kernel
-  int bn;
-  int splits;
-  int kb_total;
-  int num_m_tiles, num_n_tiles, num_tiles;
-  size_t ws_bytes;
-  size_t ws_counter_offset;
-  char name[96];
-};
 
 namespace {
 

@@ -134,6 +134,22 @@ MM4_API mm4_status mm4_gemm_partial_run(const mm4_gemm_plan* plan, const void* A
 MM4_API mm4_status mm4_splitk_finalize(int32_t M, int32_t N, const float* C32, const void* bias, void* C,
                                mm4_stream_t stream);
 
+/* Split-K GEMM that allocates no device memory: C = A*B (+bias) like
+ * mm4_gemm_run, for callers that cannot call cudaMalloc where they issue the
+ * GEMM (a framework allocator that owns all GPU memory, real-time or serving
+ * loops where an allocation may stall or fail, plug-in hosts that only pass
+ * in their input/output buffers). No reference counterpart: the reference
+ * allocates its split-K output buffer per run (matmul.swift:395-400).
+ * The fp32 partial-sum scratch is a static 4 MiB device array inside the
+ * library (held on every device that loads it until exit); plans whose
+ * mm4_gemm_workspace_size() exceeds 4 MiB, or that are not tensor-core
+ * split-K plans, are rejected. The first call on a device resolves the
+ * array's device address (make it before any stream capture). Each call
+ * clears the scratch it uses on `stream`; calls that overlap on the GPU
+ * share the scratch and race. */
+MM4_API mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* plan, const void* A, const void* B,
+                                               const void* bias, void* C, mm4_stream_t stream);
+
 /* ======================================================================== */
 /* Flash-attention forward                                                  */
 /* ======================================================================== */
