@@ -1,0 +1,85 @@
+"""Attention host interface: the reference's attention descriptors on the mm4 C ABI.
+
+Mirrors Sources/attention/attention.swift: `AttentionDimensions(R, C, K, Hq,
+Hk)` (:15-21; R = query rows, C = key/value rows, K = head dimension),
+`BlockDimenions` / `BuildOptions` (:4-13; accepted as tuning hints), and
+createSource + run(...) (:23-382, :398-541) as `AttentionPlan`. Tensors are
+fp16 torch CUDA tensors in [B][H][S][D] (BHSD) or [B][S][H][D] (BSHD, the
+reference's [S][H][D] packing with batch outermost).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+from . import _lib
+from ._lib import MM4_ATTN_BHSD, MM4_ATTN_BSHD  # noqa: F401
+
+
+@dataclass
+class AttentionDimensions:
+    R: int
+    C: int
+    K: int
+    Hq: int
+    Hk: int
+
+
+@dataclass
+class BlockDimenions:  # (sic) the reference's spelling, attention.swift:9
+    R: int = 128
+    C: int = 128
+    K: int = 128
+
+
+@dataclass
+class BuildOptions:
+    executionSIMDGroups: int = 4
+    bypassThreadgroupMemory: bool = True
+
+
+class AttentionPlan:
+    """Non-causal flash-attention forward for one (batch, dims, layout)."""
+
+    def __init__(self, dims: AttentionDimensions, batch: int = 1, layout: int = MM4_ATTN_BHSD,
+                 scale: float | None = None, blockDimensions: BlockDimenions | None = None,
+                 buildOptions: BuildOptions | None = None):
+        self._L = _lib.lib()
+        self.dims = dims
+        self.batch = batch
+        self.layout = layout
+        self.scale = scale if scale is not None else 1.0 / math.sqrt(dims.K)
+        d = _lib.AttentionDesc(batch, dims.Hq, dims.Hk, dims.R, dims.C, dims.K, float(self.scale), layout)
+        h = ctypes.c_void_p()
+        _lib.check(self._L.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(d)))
+        self._h = h
+        self.kernel_name = self._L.mm4_attention_plan_kernel_name(h).decode()
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._L.mm4_attention_plan_destroy(h)
+            self._h = None
+
+    def shape(self, rows: int, heads: int):
+        if self.layout == MM4_ATTN_BHSD:
+            return (self.batch, heads, rows, self.dims.K)
+        return (self.batch, rows, heads, self.dims.K)
+
+    def flops(self) -> float:
+        """4*B*Hq*R*C*D (two GEMMs); the reference counts (2D+5)*S^2*H (attention.swift:513)."""
+        return 4.0 * self.batch * self.dims.Hq * self.dims.R * self.dims.C * self.dims.K
+
+    def run(self, Q, K, V, O=None, stream=None, duplicatedCount: int = 1):
+        import torch
+        d = self.dims
+        for t, shp, n in ((Q, self.shape(d.R, d.Hq), "Q"), (K, self.shape(d.C, d.Hk), "K"),
+                          (V, self.shape(d.C, d.Hk), "V")):
+            if tuple(t.shape) != shp or t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{n} must be a contiguous CUDA fp16 tensor of shape {shp}")
+        if O is None:
+            O = torch.empty(self.shape(d.R, d.Hq), dtype=torch.float16, device=Q.device)
+        _lib.check(self._L.mm4_attention_fwd(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                             _lib.stream_handle(stream), int(duplicatedCount)))
+        return O
