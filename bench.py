@@ -3,17 +3,24 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl mm4|reference]
 
-Prints ONE JSON line (rank 0). A "step" is one pass of the hot path over
-one batch of synthetic input:
+Prints ONE JSON line (rank 0). A "step" is one pass of the hot path over one
+batch of synthetic input (seeded torch generators, fp16, BASELINE shapes and
+distributions):
 
   splitk (default)  BASELINE configs[1]: C = A*B + bias, M=N=512, K=65536,
                     split-K 32, fp32 partials reduced in-kernel, fp16 out.
-                    N>1: K is sharded over ranks; every rank computes its fp32
-                    partial, the partials are summed with an NCCL reduce over
+                    N>1: K is sharded over ranks; each rank computes its fp32
+                    partial, the partials are summed by an NCCL reduce over
                     NVLink and rank 0 adds bias and rounds (strong scaling).
+  splitk65520       the K=65520 variant of configs[1].
   gemm1024          BASELINE configs[0] (1024^3 GEMM+bias, NN).
-  gemm8192          the north-star target shape 8192^3 GEMM+bias, NN.
-  attention, conv2d, conv3d   BASELINE configs[2..4] (when built).
+  gemm8192          the north-star target shape, 8192^3 GEMM+bias, NN.
+  attention         BASELINE configs[2]: B=4, H=16, S=4096, D=128, non-causal.
+  conv2d            BASELINE configs[3]: N=32, 56x56, 256->256, 3x3, pad 1.
+  conv3d            BASELINE configs[4]: N=8, D=16, 64x64, 128->128, 3x3x3, pad 1.
+  For N>1 the non-split workloads are sharded with no collective: each rank
+  owns one full-size shard (N columns / batch*heads / batch), so per-GPU work
+  is fixed as N grows (weak scaling) and `value` is the whole-job rate.
 
 Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA
 events on the launching stream, with a 512 MiB write between steps to flush
@@ -21,19 +28,19 @@ L2 (126 MB) outside the events. Barrier + synchronize on both sides; the
 reported time is the max over ranks.
 
 `--impl reference` times the reference's CPU implementation of the path (the
-C restatement of its Swift validation loops, oracle/) on the host cores, on a
-bounded sample of the same workload, extrapolated to the full workload.
+C restatement of its Swift validation loops under oracle/, all host threads)
+on a bounded sample of the same workload, extrapolated to the full workload.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from pathlib import Path
 
@@ -42,31 +49,7 @@ sys.path.insert(0, str(ROOT))
 
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "dram_traffic.json"
-
-# ---------------------------------------------------------------------------
-# workloads
-# ---------------------------------------------------------------------------
-
-WORKLOADS = {
-    "splitk": dict(kind="gemm", M=512, N=512, K=65536, split=32, seed=2, bound="hbm",
-                   name="splitk_gemm_bias_512x512x65536_s32_nn", config_index=1),
-    "splitk65520": dict(kind="gemm", M=512, N=512, K=65520, split=32, seed=2, bound="hbm",
-                        name="splitk_gemm_bias_512x512x65520_s32_nn", config_index=1),
-    "gemm1024": dict(kind="gemm", M=1024, N=1024, K=1024, split=1, seed=1, bound="tensor",
-                     name="gemm_bias_1024x1024x1024_nn", config_index=0),
-    "gemm8192": dict(kind="gemm", M=8192, N=8192, K=8192, split=1, seed=11, bound="tensor",
-                     name="gemm_bias_8192x8192x8192_nn", config_index=None),
-}
-
-
-def gemm_flops(w):
-    return 2.0 * w["M"] * w["N"] * w["K"]
-
-
-def gemm_bytes(w):
-    # algorithmic: A + B + bias read once, C written once (fp16); the split-K
-    # fp32 workspace is not algorithmic traffic.
-    return 2.0 * (w["M"] * w["K"] + w["K"] * w["N"] + w["N"] + w["M"] * w["N"])
+METRIC = "TFLOP/s per GPU & % of fp16 tensor peak (GEMM/attn/conv)"
 
 
 def load_peaks():
@@ -84,6 +67,115 @@ def load_traffic(name):
         return json.loads(TRAFFIC_FILE.read_text()).get(name)
     except Exception:
         return None
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+class GemmWorkload:
+    def __init__(self, M, N, K, split, seed, bound, config_index):
+        self.M, self.N, self.K, self.split, self.seed = M, N, K, split, seed
+        self.bound = bound
+        self.config_index = config_index
+        self.name = (f"splitk_gemm_bias_{M}x{N}x{K}_s{split}_nn" if split > 1 else f"gemm_bias_{M}x{N}x{K}_nn")
+
+    def flops(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def bytes(self):
+        return 2.0 * (self.M * self.K + self.K * self.N + self.N + self.M * self.N)
+
+    def config(self):
+        return {"workload": self.name, "M": self.M, "N": self.N, "K": self.K, "split_k": self.split,
+                "layout": "row-major NN (A[M][K], B[K][N])", "bias": True, "inputs": "U[-1,1] fp16"}
+
+    def inputs(self, dev, gen):
+        import torch
+        A = (torch.rand((self.M, self.K), generator=gen, device=dev) * 2 - 1).half()
+        B = (torch.rand((self.K, self.N), generator=gen, device=dev) * 2 - 1).half()
+        bias = (torch.rand((self.N,), generator=gen, device=dev) * 2 - 1).half()
+        return {"A": A, "B": B, "bias": bias}
+
+
+class AttentionWorkload:
+    name = "attention_fwd_b4_h16_s4096_d128_noncausal"
+    bound = "tensor"
+    config_index = 2
+    B, H, S, D = 4, 16, 4096, 128
+    seed = 3
+
+    def flops(self):
+        return 4.0 * self.B * self.H * self.S * self.S * self.D
+
+    def bytes(self):
+        return 4.0 * self.B * self.H * self.S * self.D * 2
+
+    def config(self):
+        return {"workload": self.name, "batch": self.B, "heads": self.H, "seq_len": self.S, "head_dim": self.D,
+                "layout": "[B][H][S][D]", "scale": 1 / math.sqrt(self.D), "inputs": "N(0,1) fp16",
+                "reference_flop_count_(2D+5)S^2H": (2 * self.D + 5) * self.S * self.S * self.H * self.B}
+
+    def inputs(self, dev, gen):
+        import torch
+        shp = (self.B, self.H, self.S, self.D)
+        return {k: torch.randn(shp, generator=gen, device=dev).half() for k in ("Q", "K", "V")}
+
+
+class ConvWorkload:
+    def __init__(self, three_d):
+        self.three_d = three_d
+        if three_d:
+            self.name = "conv3d_ndhwc_n8_d16_64x64_c128_k128_3x3x3_pad1"
+            self.config_index = 4
+            self.N, self.D, self.H, self.W, self.C, self.O, self.k = 8, 16, 64, 64, 128, 128, 3
+            self.wsig, self.seed = 0.03, 5
+        else:
+            self.name = "conv2d_nhwc_n32_56x56_c256_k256_3x3_pad1"
+            self.config_index = 3
+            self.N, self.D, self.H, self.W, self.C, self.O, self.k = 32, 1, 56, 56, 256, 256, 3
+            self.wsig, self.seed = 0.05, 4
+        self.bound = "tensor"
+
+    def taps(self):
+        return self.k ** 3 if self.three_d else self.k ** 2
+
+    def flops(self):
+        return 2.0 * self.N * self.D * self.H * self.W * self.O * self.taps() * self.C
+
+    def bytes(self):
+        return 2.0 * (self.N * self.D * self.H * self.W * (self.C + self.O) + self.O * self.taps() * self.C + self.O)
+
+    def config(self):
+        c = {"workload": self.name, "batch": self.N, "H": self.H, "W": self.W, "Cin": self.C, "Cout": self.O,
+             "kernel": self.k, "stride": 1, "padding": 1, "bias": True,
+             "layout": "NDHWC x [Cout][3][3][3][Cin]" if self.three_d else "NHWC x [Cout][3][3][Cin]",
+             "inputs": f"x N(0,1), w N(0,{self.wsig}), bias U[-0.1,0.1], fp16"}
+        if self.three_d:
+            c["D"] = self.D
+        return c
+
+    def weight_shape(self):
+        return (self.O, self.k, self.k, self.k, self.C) if self.three_d else (self.O, self.k, self.k, self.C)
+
+    def inputs(self, dev, gen):
+        import torch
+        xs = (self.N, self.D, self.H, self.W, self.C) if self.three_d else (self.N, self.H, self.W, self.C)
+        x = torch.randn(xs, generator=gen, device=dev).half()
+        w = (torch.randn(self.weight_shape(), generator=gen, device=dev) * self.wsig).half()
+        bias = ((torch.rand((self.O,), generator=gen, device=dev) * 2 - 1) * 0.1).half()
+        return {"x": x, "w": w, "bias": bias}
+
+
+WORKLOADS = {
+    "splitk": lambda: GemmWorkload(512, 512, 65536, 32, 2, "hbm", 1),
+    "splitk65520": lambda: GemmWorkload(512, 512, 65520, 32, 2, "hbm", 1),
+    "gemm1024": lambda: GemmWorkload(1024, 1024, 1024, 1, 1, "tensor", 0),
+    "gemm8192": lambda: GemmWorkload(8192, 8192, 8192, 1, 11, "tensor", None),
+    "attention": AttentionWorkload,
+    "conv2d": lambda: ConvWorkload(False),
+    "conv3d": lambda: ConvWorkload(True),
+}
 
 
 # ---------------------------------------------------------------------------
@@ -114,7 +206,7 @@ class Dist:
         if not self.pg:
             return value
         import torch
-        t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -170,37 +262,27 @@ class ClockSampler:
         os.unlink(self.file.name)
         if not rows:
             return None
+        loaded = [r for r in rows if r["power"] > 250.0] or rows
         reasons = set()
         for r in rows:
             for key, name in (("hw", "hw_slowdown"), ("hw_thermal", "hw_thermal_slowdown"),
                               ("sw_thermal", "sw_thermal_slowdown"), ("sw_power", "sw_power_cap")):
                 if r[key].lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": max(r["max"] for r in rows),
-                "power_w_max": max(r["power"] for r in rows), "samples": len(rows), "reasons": sorted(reasons)}
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["max"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows), "samples": len(rows),
+                "samples_under_load": len(loaded), "reasons": sorted(reasons)}
 
 
 # ---------------------------------------------------------------------------
-# inputs
-# ---------------------------------------------------------------------------
-
-def gemm_inputs(w, tl=False, tr=False):
-    """Seeded U[-1,1] fp16 A[M][K], B[K][N], bias[N]."""
-    from example_matmul_metal4_b200 import data
-    A = data.uniform((w["M"], w["K"]), -1.0, 1.0, w["seed"], 0)
-    B = data.uniform((w["K"], w["N"]), -1.0, 1.0, w["seed"], 1)
-    bias = data.uniform((w["N"],), -1.0, 1.0, w["seed"], 2)
-    return A, B, bias
-
-
-# ---------------------------------------------------------------------------
-# mm4 arm
+# timing helpers
 # ---------------------------------------------------------------------------
 
 def time_steps(step, steps, warmup, flush, stream, dist):
     """Per-step CUDA events on `stream`; L2 flush between steps outside events."""
     import torch
     for _ in range(warmup):
+        flush.zero_()
         step()
     torch.cuda.synchronize()
     dist.barrier()
@@ -217,8 +299,7 @@ def time_steps(step, steps, warmup, flush, stream, dist):
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    per_step = [s.elapsed_time(e) for s, e in events]
-    return per_step
+    return [s.elapsed_time(e) for s, e in events]
 
 
 def burn(step, flush, seconds):
@@ -226,147 +307,236 @@ def burn(step, flush, seconds):
     import torch
     t_end = time.perf_counter() + seconds
     while time.perf_counter() < t_end:
-        for _ in range(8):
+        for _ in range(4):
             flush.zero_()
             step()
         torch.cuda.synchronize()
 
 
-def run_gemm_mm4(args, w, dist, peaks):
+# ---------------------------------------------------------------------------
+# mm4 arm: per-workload step builders
+# Each returns (step, e2e_step, (h2d, d2h) bytes, kernel name, launches/step, scaling).
+# ---------------------------------------------------------------------------
+
+def build_gemm(w, dist, dev, gen):
     import torch
-    from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan, lib, sync_check
+    from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan
     from example_matmul_metal4_b200.gemm import splitk_finalize
-
-    dev = torch.device("cuda", dist.local_rank)
-    torch.cuda.set_device(dev)
-    dist.init("nccl")
-    stream = torch.cuda.current_stream()
-    A, B, bias = gemm_inputs(w)
-    M, N, K = w["M"], w["N"], w["K"]
     P, r = dist.world, dist.rank
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
-    launches_per_step = 1
-
-    if P == 1:
-        plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
-                        buildOptions=BuildOptions(splitK=w["split"]))
-        tA, tB, tb = (torch.from_numpy(x).to(dev) for x in (A, B, bias))
+    M, N, K = w.M, w.N, w.K
+    if P > 1 and w.split > 1:
+        # K shards of one problem + fp32 NCCL reduce to rank 0 + bias/cast there.
+        from example_matmul_metal4_b200.parallel import k_shard, reduce_partials, splitk_per_rank
+        k0, k1 = k_shard(K, P, r)
+        full = w.inputs(dev, gen)  # identical on every rank (same seed)
+        A = full["A"][:, k0:k1].contiguous()
+        B = full["B"][k0:k1].contiguous()
+        bias = full["bias"]
+        del full
+        plan = GemmPlan(GEMMDimensions(M, N, k1 - k0), transpose=(False, False), bias=False,
+                        buildOptions=BuildOptions(splitK=splitk_per_rank(w.split, P)))
+        C32 = torch.empty((M, N), dtype=torch.float32, device=dev)
         C = torch.empty((M, N), dtype=torch.float16, device=dev)
         ws = plan.workspace(dev)
 
         def step():
-            plan.run(tA, tB, tb, C=C, workspace=ws)
-        kernel_name = plan.kernel_name
+            plan.partial(A, B, C32=C32, workspace=ws)
+            reduce_partials(C32, dst=0)
+            if r == 0:
+                splitk_finalize(C32, bias, C=C)
+        return step, None, None, plan.kernel_name + " + nccl reduce + finalize", (2 if r == 0 else 1), "strong"
+    t = w.inputs(dev, gen)
+    A, B, bias = t["A"], t["B"], t["bias"]
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
+                    buildOptions=BuildOptions(splitK=w.split))
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    ws = plan.workspace(dev)
+
+    def step():
+        plan.run(A, B, bias, C=C, workspace=ws)
+
+    hA, hB, hb = A.cpu().pin_memory(), B.cpu().pin_memory(), bias.cpu().pin_memory()
+    hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        A.copy_(hA, non_blocking=True)
+        B.copy_(hB, non_blocking=True)
+        bias.copy_(hb, non_blocking=True)
+        plan.run(A, B, bias, C=C, workspace=ws)
+        hC.copy_(C, non_blocking=True)
+    e2e_bytes = (A.numel() * 2 + B.numel() * 2 + bias.numel() * 2, C.numel() * 2)
+    return step, e2e_step, e2e_bytes, plan.kernel_name, 1, "weak"
+
+
+def build_attention(w, dist, dev, gen):
+    import torch
+    from example_matmul_metal4_b200.attention import AttentionDimensions, AttentionPlan
+    plan = AttentionPlan(AttentionDimensions(w.S, w.S, w.D, w.H, w.H), batch=w.B)
+    t = w.inputs(dev, gen)
+    Q, K, V = t["Q"], t["K"], t["V"]
+    O = torch.empty_like(Q)
+
+    def step():
+        plan.run(Q, K, V, O=O)
+
+    hQ, hK, hV = Q.cpu().pin_memory(), K.cpu().pin_memory(), V.cpu().pin_memory()
+    hO = torch.empty(O.shape, dtype=O.dtype).pin_memory()
+
+    def e2e_step():
+        Q.copy_(hQ, non_blocking=True)
+        K.copy_(hK, non_blocking=True)
+        V.copy_(hV, non_blocking=True)
+        plan.run(Q, K, V, O=O)
+        hO.copy_(O, non_blocking=True)
+    return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "weak"
+
+
+def build_conv(w, dist, dev, gen):
+    import torch
+    from example_matmul_metal4_b200.conv import (WEIGHTS_ODHWI, WEIGHTS_OHWI, Conv2DDimensions, Conv3DDimensions,
+                                                 ConvPlan)
+    if w.three_d:
+        dims = Conv3DDimensions(w.N, w.D, w.H, w.W, w.C, w.O, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1)
+        plan = ConvPlan(dims, weight_layout=WEIGHTS_ODHWI, bias=True)
     else:
-        if w["split"] <= 1:
-            # N-column shards, no collective (weak in N: every rank owns N columns).
-            plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
-                            buildOptions=BuildOptions(splitK=1))
-            tA, tB, tb = (torch.from_numpy(x).to(dev) for x in (A, B, bias))
-            C = torch.empty((M, N), dtype=torch.float16, device=dev)
+        dims = Conv2DDimensions(w.N, w.H, w.W, w.C, w.O, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1)
+        plan = ConvPlan(dims, weight_layout=WEIGHTS_OHWI, bias=True)
+    t = w.inputs(dev, gen)
+    x, wt, bias = t["x"], t["w"], t["bias"]
+    y = torch.empty(plan.out_shape, dtype=torch.float16, device=dev)
 
-            def step():
-                plan.run(tA, tB, tb, C=C)
-            kernel_name = plan.kernel_name
-        else:
-            # K shards + fp32 NCCL reduce to rank 0 + bias/cast on rank 0.
-            k0, k1 = (K * r) // P, (K * (r + 1)) // P
-            shard_split = max(1, w["split"] // P)
-            plan = GemmPlan(GEMMDimensions(M, N, k1 - k0), transpose=(False, False), bias=False,
-                            buildOptions=BuildOptions(splitK=shard_split))
-            tA = torch.from_numpy(A[:, k0:k1].copy()).to(dev)
-            tB = torch.from_numpy(B[k0:k1].copy()).to(dev)
-            tb = torch.from_numpy(bias).to(dev)
-            C32 = torch.empty((M, N), dtype=torch.float32, device=dev)
-            C = torch.empty((M, N), dtype=torch.float16, device=dev)
-            ws = plan.workspace(dev)
-            import torch.distributed as tdist
+    def step():
+        plan.run(x, wt, bias, y=y)
 
-            def step():
-                plan.partial(tA, tB, C32=C32, workspace=ws)
-                tdist.reduce(C32, dst=0, op=tdist.ReduceOp.SUM)
-                if r == 0:
-                    splitk_finalize(C32, tb, C=C)
-            launches_per_step = 2 if r == 0 else 1
-            kernel_name = plan.kernel_name + "+nccl_reduce+finalize"
+    hx, hw, hb = x.cpu().pin_memory(), wt.cpu().pin_memory(), bias.cpu().pin_memory()
+    hy = torch.empty(plan.out_shape, dtype=torch.float16).pin_memory()
 
-    # correctness spot-check outside timing (rank 0 full output vs fp32 cuBLAS)
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        wt.copy_(hw, non_blocking=True)
+        bias.copy_(hb, non_blocking=True)
+        plan.run(x, wt, bias, y=y)
+        hy.copy_(y, non_blocking=True)
+    return step, e2e_step, ((x.numel() + wt.numel() + bias.numel()) * 2, y.numel() * 2), plan.kernel_name, 1, "weak"
+
+
+def run_mm4(args, w, dist, peaks):
+    import torch
+    from example_matmul_metal4_b200 import sync_check
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    dist.init("nccl")
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev)
+    same_inputs = isinstance(w, GemmWorkload) and w.split > 1
+    gen.manual_seed(w.seed * 1000003 + (0 if same_inputs else dist.rank))
+    builder = (build_gemm if isinstance(w, GemmWorkload) else
+               build_attention if isinstance(w, AttentionWorkload) else build_conv)
+    step, e2e_step, e2e_bytes, kernel_name, launches, scaling = builder(w, dist, dev, gen)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+
     step()
     torch.cuda.synchronize()
     sync_check()
 
     clocks = ClockSampler(dist.local_rank)
     clocks.start()
-    burn(step, flush, 0.6)  # load the GPU so the sampler sees clocks under load
+    burn(step, flush, 0.6)
     per_step = time_steps(step, args.steps, args.warmup, flush, stream, dist)
     burn(step, flush, 0.3)
     clk = clocks.stop()
+    sync_check()
     ms = dist.max(sum(per_step) / len(per_step))
 
-    flops = gemm_flops(w)
-    value = flops / (ms * 1e-3) / 1e12  # whole-job TFLOP/s (one problem per step across all ranks)
+    units = 1 if scaling == "strong" else dist.world  # full-size problems completed per step, whole job
+    value = units * w.flops() / (ms * 1e-3) / 1e12
 
-    # e2e through the public API from pinned host buffers (rank 0, single GPU)
     e2e = None
-    if P == 1:
-        hA = torch.from_numpy(A).pin_memory()
-        hB = torch.from_numpy(B).pin_memory()
-        hb = torch.from_numpy(bias).pin_memory()
-        hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
-
-        def e2e_step():
-            tA.copy_(hA, non_blocking=True)
-            tB.copy_(hB, non_blocking=True)
-            tb.copy_(hb, non_blocking=True)
-            plan.run(tA, tB, tb, C=C, workspace=ws)
-            hC.copy_(C, non_blocking=True)
-        e2e_ms = sum(time_steps(e2e_step, max(3, args.steps // 2), 2, flush, stream, dist)) / max(3, args.steps // 2)
-        h2d = A.nbytes + B.nbytes + bias.nbytes
-        e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(M * N * 2)}
+    if e2e_step is not None:
+        n_e2e = max(3, args.steps // 2)
+        e2e_ms = dist.max(sum(time_steps(e2e_step, n_e2e, 2, flush, stream, dist)) / n_e2e)
+        e2e = {"value": units * w.flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(e2e_bytes[0]), "d2h_bytes_per_step": int(e2e_bytes[1])}
 
     roof = None
-    if P == 1:
-        if w["bound"] == "hbm":
-            achieved = gemm_bytes(w) / (ms * 1e-3) / 1e9
-            peak = peaks["hbm_gbs"]
-            unit = "GB/s"
+    if dist.world == 1:
+        if w.bound == "hbm":
+            achieved, peak, unit = w.bytes() / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
         else:
-            achieved = value
-            peak = peaks["bf16_tflops"]
-            unit = "TFLOP/s"
-        roof = {"bound": w["bound"], "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
-                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json)" if peaks["source"] == "measured"
-                else "fallback", "algorithmic_bytes": gemm_bytes(w), "algorithmic_flops": flops,
-                "traffic": load_traffic(w["name"]), "kernel": kernel_name}
-    return dict(value=value, ms=ms, clocks=clk, e2e=e2e, roofline=roof, launches=launches_per_step * args.steps,
-                kernel=kernel_name, flops=flops, pct_of_bf16_peak=value / peaks["bf16_tflops"])
+            achieved, peak, unit = value, peaks["bf16_tflops"], "TFLOP/s"
+        roof = {"bound": w.bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+                "peak_source": ("measured, MEASURED_PEAKS.json (burst)" if peaks["source"] == "measured"
+                                else "fallback"),
+                "algorithmic_bytes": w.bytes(), "algorithmic_flops": w.flops(),
+                "traffic": load_traffic(w.name), "kernel": kernel_name, "kernel_ms": ms}
+    return dict(value=value, ms=ms, clocks=clk, e2e=e2e, roofline=roof, launches=launches * args.steps,
+                kernel=kernel_name, scaling=scaling)
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (the reference's CPU loops, restated in oracle/)
+# CPU legs (oracle = the reference's CPU loops restated in C)
 # ---------------------------------------------------------------------------
 
-def cpu_gemm_sample(w, seconds_hint=10.0, threads=None):
-    """Times the oracle on a bounded row sample and extrapolates to the full GEMM."""
+def cpu_sample(w, seconds_hint=10.0, threads=None):
+    """Times the oracle on a bounded sample of workload `w`, extrapolated to the full workload."""
     sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
     import oracle
     threads = threads or oracle.max_threads()
-    A, B, bias = gemm_inputs(w)
-    M, N, K = w["M"], w["N"], w["K"]
-    # calibrate with one row, then size the sample to ~seconds_hint
-    t0 = time.perf_counter()
-    oracle.gemm(A, B, bias, M, N, K, False, False, rows=(0, 1), threads=1)
-    one_row = time.perf_counter() - t0
-    rows = int(max(threads, min(M, seconds_hint * threads / max(one_row, 1e-6))))
-    rows = max(1, min(M, (rows // threads) * threads or threads))
-    t0 = time.perf_counter()
-    oracle.gemm(A, B, bias, M, N, K, False, False, rows=(0, rows), threads=threads)
-    dt = time.perf_counter() - t0
-    flops = 2.0 * rows * N * K
+    rng = np.random.default_rng(12345)
+
+    def timed(fn):
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    def h(shape, scale=1.0, uniform=False):
+        if uniform:
+            a = rng.uniform(-scale, scale, size=shape).astype(np.float32)
+        else:
+            a = rng.standard_normal(shape, dtype=np.float32) * scale
+        return a.astype(np.float16)
+
+    if isinstance(w, GemmWorkload):
+        M, N, K = w.M, w.N, w.K
+        A, B, bias = h((M, K), uniform=True), h((K, N), uniform=True), h((N,), uniform=True)
+        one = timed(lambda: oracle.gemm(A, B, bias, M, N, K, rows=(0, 1), threads=1))
+        rows = max(1, min(M, int(seconds_hint * threads / max(one, 1e-6))))
+        dt = timed(lambda: oracle.gemm(A, B, bias, M, N, K, rows=(0, rows), threads=threads))
+        flops = 2.0 * rows * N * K
+        sample = (f"{rows} of {M} output rows of the {M}x{N}x{K} GEMM+bias (fp32 loop of matmul.swift:499-510), "
+                  f"{dt:.2f} s")
+    elif isinstance(w, AttentionWorkload):
+        S, D = w.S, w.D
+        H = threads  # one head per thread, a block of query rows of each
+        Q, Kt, V = h((1, H, S, D)), h((1, H, S, D)), h((1, H, S, D))
+        one = timed(lambda: oracle.attention(Q, Kt, V, 1, 1, 1, S, S, D, 1 / math.sqrt(D), rows=(0, 1), threads=1))
+        rows = max(1, min(S, int(seconds_hint / max(one, 1e-6))))
+        dt = timed(lambda: oracle.attention(Q, Kt, V, 1, H, H, S, S, D, 1 / math.sqrt(D), rows=(0, rows),
+                                            threads=threads))
+        flops = 4.0 * H * rows * S * D
+        sample = (f"{rows} query rows x {H} heads of S={S}, D={D} attention (Network.swift:134-179, :286-311), "
+                  f"{dt:.2f} s")
+    else:
+        b = np.zeros(w.O, dtype=np.float16)
+        if w.three_d:
+            x, wt = h((1, w.D, w.H, w.W, w.C)), h((w.O, 3, 3, 3, w.C), w.wsig)
+            kw = dict(N=1, D=w.D, H=w.H, W=w.W, C=w.C, O=w.O, KD=3, KH=3, KW=3, pad_front=1, pad_back=1,
+                      pad_top=1, pad_bottom=1, pad_left=1, pad_right=1, layout=4)
+            total_rows, per_row_flops, fn = w.D * w.H, 2.0 * w.W * w.O * 27 * w.C, oracle.conv3d
+        else:
+            x, wt = h((1, w.H, w.W, w.C)), h((w.O, 3, 3, w.C), w.wsig)
+            kw = dict(N=1, H=w.H, W=w.W, C=w.C, O=w.O, KH=3, KW=3, pad_top=1, pad_bottom=1, pad_left=1,
+                      pad_right=1, layout=1)
+            total_rows, per_row_flops, fn = w.H, 2.0 * w.W * w.O * 9 * w.C, oracle.conv2d
+        one = timed(lambda: fn(x, wt, b, rows=(0, 1), threads=1, **kw))
+        rows = max(1, min(total_rows, int(seconds_hint * threads / max(one, 1e-6))))
+        dt = timed(lambda: fn(x, wt, b, rows=(0, rows), threads=threads, **kw))
+        flops = per_row_flops * rows
+        sample = (f"{rows} output rows ({w.W} pixels x {w.O} channels each) of one image of the {w.name} conv "
+                  f"(ConvolutionShared.swift:4994-5096), {dt:.2f} s")
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {M} output rows of the {M}x{N}x{K} GEMM+bias (fp32 loop of matmul.swift:499-510), "
-                      f"{dt:.2f} s, extrapolated linearly"}
+            "sample": sample + ", extrapolated linearly to the full workload"}
 
 
 # ---------------------------------------------------------------------------
@@ -381,53 +551,48 @@ def main():
     ap.add_argument("--workload", default="splitk", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mm4", choices=["mm4", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
-    if args.warmup < 3:
-        args.warmup = 3
-    w = WORKLOADS[args.workload]
+    args.warmup = max(3, args.warmup)
+    w = WORKLOADS[args.workload]()
     dist = Dist(args.gpus)
     peaks = load_peaks()
-
-    base = {"metric": "TFLOP/s per GPU & % of fp16 tensor peak (GEMM/attn/conv)", "unit": "TFLOP/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)", "data": "synthetic (seeded Philox, U[-1,1])"}
+    base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
+            "data": "synthetic (seeded torch generator; BASELINE shapes and distributions)"}
+    cfg = dict(w.config(), l2="flushed between steps (512 MiB write outside the timed events)",
+               baseline_config_index=w.config_index)
 
     if args.impl == "reference":
         if dist.rank != 0:
             return
-        cores = None
-        vals = []
-        sample = None
+        vals, cb = [], None
+        per_step = max(1.0, min(8.0, 120.0 / (args.warmup + args.steps)))
         for i in range(args.warmup + args.steps):
-            cb = cpu_gemm_sample(w, seconds_hint=2.0 if i >= args.warmup else 0.5, threads=cores)
-            cores = cb["cores"]
-            sample = cb["sample"]
+            cb = cpu_sample(w, seconds_hint=per_step if i >= args.warmup else 0.5)
             if i >= args.warmup:
                 vals.append(cb["value"])
         value = statistics.mean(vals)
-        line = dict(base, impl="reference", value=value, ms_per_step=gemm_flops(w) / (value * 1e12) * 1e3,
-                    scaling="strong", config={"workload": w["name"], "M": w["M"], "N": w["N"], "K": w["K"],
-                                              "split_k": w["split"], "l2": "n/a (CPU)"},
-                    cpu_baseline={"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        line = dict(base, impl="reference", value=value, ms_per_step=w.flops() / (value * 1e12) * 1e3,
+                    scaling="strong", config=dict(cfg, l2="n/a (host CPU)"),
+                    cpu_baseline={"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
+                                  "sample": cb["sample"]},
                     e2e={"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                     gpu_launches=0)
         print(json.dumps(line), flush=True)
         return
 
-    res = run_gemm_mm4(args, w, dist, peaks)
+    res = run_mm4(args, w, dist, peaks)
     if dist.rank == 0:
         cpu = None
         if args.gpus == 1 and not args.no_cpu_baseline:
-            cpu = cpu_gemm_sample(w, seconds_hint=10.0)
-        line = dict(base, value=res["value"], ms_per_step=res["ms"],
-                    scaling="strong" if (args.gpus > 1 and w["split"] > 1) else "weak",
-                    config={"workload": w["name"], "M": w["M"], "N": w["N"], "K": w["K"], "split_k": w["split"],
-                            "layout": "row-major NN (A[M][K], B[K][N])", "bias": True,
-                            "l2": "flushed between steps (512 MiB write outside the timed events)",
-                            "kernel": res["kernel"],
-                            "parallelism": ("K-shard + NCCL fp32 reduce" if w["split"] > 1 else "N-column shards")
-                            if args.gpus > 1 else "single GPU"},
-                    pct_of_measured_bf16_peak=res["pct_of_bf16_peak"],
+            cpu = cpu_sample(w, seconds_hint=args.cpu_seconds)
+        cfg["kernel"] = res["kernel"]
+        cfg["parallelism"] = ("single GPU" if args.gpus == 1 else
+                              ("K-shard + NCCL fp32 reduce" if res["scaling"] == "strong" else
+                               f"{args.gpus} independent shards, no collective"))
+        line = dict(base, value=res["value"], ms_per_step=res["ms"], scaling=res["scaling"], config=cfg,
+                    pct_of_measured_bf16_peak=res["value"] / args.gpus / peaks["bf16_tflops"],
                     clocks=res["clocks"], e2e=res["e2e"], roofline=res["roofline"], cpu_baseline=cpu,
                     gpu_launches=res["launches"])
         print(json.dumps(line), flush=True)

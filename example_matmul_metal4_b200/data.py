@@ -23,14 +23,11 @@ _W1 = np.uint32(0xBB67AE85)
 _MASK32 = np.uint64(0xFFFFFFFF)
 
 
-def philox4x32(counter_lo: np.ndarray, counter_hi: np.ndarray, tensor_id: int, seed: int) -> tuple[np.ndarray, ...]:
-    """Philox-4x32-10 on counters (lo, hi, tensor_id, 0) with key (seed, seed >> 32)."""
-    c0 = counter_lo.astype(np.uint32)
-    c1 = counter_hi.astype(np.uint32)
-    c2 = np.full_like(c0, np.uint32(tensor_id & 0xFFFFFFFF))
-    c3 = np.zeros_like(c0)
-    k0 = np.uint32(seed & 0xFFFFFFFF)
-    k1 = np.uint32((seed >> 32) & 0xFFFFFFFF)
+def philox4x32_10(c0, c1, c2, c3, k0: int, k1: int) -> tuple[np.ndarray, ...]:
+    """Philox-4x32-10 block function on uint32 counter arrays (c0..c3) and key (k0, k1)."""
+    c0, c1, c2, c3 = (np.asarray(c, dtype=np.uint32) for c in (c0, c1, c2, c3))
+    k0 &= 0xFFFFFFFF
+    k1 &= 0xFFFFFFFF
     for _ in range(10):
         p0 = c0.astype(np.uint64) * _M0
         p1 = c2.astype(np.uint64) * _M1
@@ -38,10 +35,17 @@ def philox4x32(counter_lo: np.ndarray, counter_hi: np.ndarray, tensor_id: int, s
         lo0 = (p0 & _MASK32).astype(np.uint32)
         hi1 = (p1 >> np.uint64(32)).astype(np.uint32)
         lo1 = (p1 & _MASK32).astype(np.uint32)
-        c0, c1, c2, c3 = hi1 ^ c1 ^ k0, lo1, hi0 ^ c3 ^ k1, lo0
-        k0 = np.uint32((int(k0) + int(_W0)) & 0xFFFFFFFF)
-        k1 = np.uint32((int(k1) + int(_W1)) & 0xFFFFFFFF)
+        c0, c1, c2, c3 = hi1 ^ c1 ^ np.uint32(k0), lo1, hi0 ^ c3 ^ np.uint32(k1), lo0
+        k0 = (k0 + int(_W0)) & 0xFFFFFFFF
+        k1 = (k1 + int(_W1)) & 0xFFFFFFFF
     return c0, c1, c2, c3
+
+
+def philox4x32(counter_lo: np.ndarray, counter_hi: np.ndarray, tensor_id: int, seed: int) -> tuple[np.ndarray, ...]:
+    """Philox-4x32-10 on counters (lo, hi, tensor_id, 0) with key (seed, seed >> 32)."""
+    lo = np.asarray(counter_lo, dtype=np.uint32)
+    return philox4x32_10(lo, counter_hi, np.full_like(lo, np.uint32(tensor_id & 0xFFFFFFFF)), np.zeros_like(lo),
+                         seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)
 
 
 def _random_words(n: int, tensor_id: int, seed: int) -> np.ndarray:

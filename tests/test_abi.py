@@ -1,0 +1,104 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol
+include/mm4.h declares, and validates descriptors on the host. No compute
+call is made here."""
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from example_matmul_metal4_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared_symbols():
+    text = (ROOT / "include" / "mm4.h").read_text()
+    return sorted(set(re.findall(r"MM4_API\s+[\w\s\*]+?\b(mm4_\w+)\s*\(", text)))
+
+
+def test_library_loads_without_gpu_runtime_dependencies():
+    lib = _lib.lib()
+    assert lib.mm4_version() >= 100
+    deps = subprocess.run(["ldd", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in deps and "libcudart" not in deps
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    syms = _declared_symbols()
+    assert len(syms) >= 25
+    lib = _lib.lib()
+    for s in syms:
+        assert hasattr(lib, s), s
+        assert s in _lib.SIGNATURES, f"{s} has no ctypes signature"
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (mm4_\w+)", nm))
+    assert set(syms) <= exported
+    assert exported <= set(syms), f"undeclared exports: {exported - set(syms)}"
+
+
+def test_status_strings():
+    lib = _lib.lib()
+    for code, name in [(0, b"MM4_OK"), (1, b"MM4_ERR_INVALID"), (5, b"MM4_ERR_TIMEOUT"), (6, b"MM4_ERR_WORKSPACE")]:
+        assert lib.mm4_status_string(code) == name
+
+
+def _gemm(**kw):
+    d = _lib.GemmDesc(*(kw.get(n, v) for n, v in [("M", 64), ("N", 64), ("K", 64), ("transpose_left", 0),
+                                                   ("transpose_right", 0), ("bias", 1), ("split_k", 1),
+                                                   ("block_m", 0), ("block_n", 0), ("block_k", 0),
+                                                   ("cooperative_simdgroups", 4), ("preemptive_simdgroups", 1),
+                                                   ("swap_mn", 0)]))
+    h = ctypes.c_void_p()
+    rc = _lib.lib().mm4_gemm_plan_create(ctypes.byref(h), ctypes.byref(d))
+    return rc, h
+
+
+def test_gemm_plan_validation_and_dispatch():
+    lib = _lib.lib()
+    assert _gemm(M=0)[0] == _lib.MM4_ERR_INVALID
+    assert _gemm(K=-3)[0] == _lib.MM4_ERR_INVALID
+    assert _gemm(transpose_left=2)[0] == _lib.MM4_ERR_INVALID
+    assert b"positive" in lib.mm4_last_error() or b"0 or 1" in lib.mm4_last_error()
+    rc, h = _gemm(M=512, N=512, K=65536, split_k=32)
+    assert rc == 0
+    assert b"splitk" in lib.mm4_gemm_plan_kernel_name(h)
+    # fp32 [4*128][2*256] workspace + 8 tile counters, rounded to 256 bytes
+    assert lib.mm4_gemm_workspace_size(h) == ((512 * 512 * 4 + 8 * 4 + 255) // 256) * 256
+    lib.mm4_gemm_plan_destroy(h)
+    rc, h = _gemm(M=33, N=40, K=31, transpose_right=1)
+    assert rc == 0 and b"simt" in lib.mm4_gemm_plan_kernel_name(h)
+    assert lib.mm4_gemm_workspace_size(h) == 0
+    lib.mm4_gemm_plan_destroy(h)
+
+
+def test_conv_and_attention_plan_validation():
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    d2 = _lib.Conv2dDesc(1, 5, 5, 4, 8, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_HWIO, 0)
+    assert lib.mm4_conv2d_plan_create(ctypes.byref(h), ctypes.byref(d2)) == 0
+    assert lib.mm4_conv_output_elements(h) == 5 * 5 * 8
+    lib.mm4_conv_plan_destroy(h)
+    bad = _lib.Conv2dDesc(1, 5, 5, 4, 8, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_DHWIO, 0)
+    assert lib.mm4_conv2d_plan_create(ctypes.byref(h), ctypes.byref(bad)) == _lib.MM4_ERR_INVALID
+    empty = _lib.Conv2dDesc(1, 2, 2, 4, 8, 3, 3, 1, 1, 1, 1, 0, 0, 0, 0, _lib.WEIGHTS_HWIO, 0)
+    assert lib.mm4_conv2d_plan_create(ctypes.byref(h), ctypes.byref(empty)) == _lib.MM4_ERR_INVALID
+    d3 = _lib.Conv3dDesc(8, 16, 64, 64, 128, 128, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_ODHWI, 1)
+    assert lib.mm4_conv3d_plan_create(ctypes.byref(h), ctypes.byref(d3)) == 0
+    assert lib.mm4_conv_output_elements(h) == 8 * 16 * 64 * 64 * 128
+    lib.mm4_conv_plan_destroy(h)
+    a = _lib.AttentionDesc(4, 16, 16, 4096, 4096, 128, 0.0, _lib.MM4_ATTN_BHSD)
+    assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == 0
+    lib.mm4_attention_plan_destroy(h)
+    a = _lib.AttentionDesc(1, 6, 4, 64, 64, 128, 0.0, _lib.MM4_ATTN_BHSD)
+    assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == _lib.MM4_ERR_INVALID
+    a = _lib.AttentionDesc(1, 4, 4, 64, 64, 96, 0.0, _lib.MM4_ATTN_BHSD)
+    assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == _lib.MM4_ERR_UNSUPPORTED
+
+
+def test_no_device_means_not_supported():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert _lib.lib().mm4_device_supported() == 0
