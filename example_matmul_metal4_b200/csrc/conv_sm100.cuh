@@ -16,14 +16,24 @@
 //   warp 0     weights producer (TMA) when the weights are 16-byte pitched
 //   warp 1     TMEM alloc + tcgen05.mma issuer        (shared with the GEMM)
 //   warps 2-5  epilogue: bias, fp16, NDHWC store      (shared with the GEMM)
+//   For stride-1 convolutions with 16-byte-pitched channels, warp 0 also
+//   loads the activations by TMA: a tile is a TH x TW rectangle of output
+//   pixels (TW*TH = 128) of one (n, oz) plane, so each tap's A operand is one
+//   5-D box {64 channels, TW, TH, 1, 1} of the NDHWC input at the tap-shifted
+//   origin, with out-of-range (padding) coordinates zero-filled by TMA.
+//   Otherwise:
 //   warps 6-9  activation gather: each thread owns one 16-byte channel chunk
 //              of 8 tile rows and copies it with cp.async (zero-filled when
 //              the tap falls in the padding or past Cin). Replaces the
 //              reference's clamp + set_offsets padding rule
 //              (AGENTS.md:76-84): out-of-range taps simply read zeros.
-// The gather threads keep LAG stages of cp.async groups in flight, and
-// publish a stage only after its group completed and a proxy fence, so the
-// tensor core (async proxy) sees the generic-proxy writes.
+// With 16-byte-aligned channels and TMA weights, the gather threads arrive on
+// a stage's mbarrier with cp.async.mbarrier.arrive.noinc (the arrival fires
+// when the thread's copies land), so up to STAGES stages are in flight with
+// no producer-side waits; the MMA thread issues fence.proxy.async after its
+// wait so the tensor core (async proxy) observes the cp.async writes. Shapes
+// that need ordinary shared-memory stores (unaligned channels or gathered
+// weights) complete their writes, fence, and arrive synchronously.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -58,6 +68,12 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint3
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Arrives on the mbarrier once all cp.async issued so far by this thread have
+// landed; counts as one of the barrier's expected arrivals (.noinc).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -75,12 +91,33 @@ __device__ __forceinline__ long long conv_weight_offset(const ConvGeom& g, int o
   }
 }
 
-template <int BN, bool B_TMA, bool B_MN>
+// Tile origin (in input coordinates, before the tap offset) of an output
+// rectangle tile when activations are TMA-fed (stride 1).
+struct ConvTileOrigin {
+  int n, z, y, x;
+};
+
+__device__ __forceinline__ ConvTileOrigin conv_tile_origin(const GemmArgs& a, const ConvGeom& g, int mt) {
+  int t = mt;
+  const int twi = t % a.rm_tiles_w;
+  t /= a.rm_tiles_w;
+  const int thi = t % a.rm_tiles_h;
+  t /= a.rm_tiles_h;
+  const int oz = t % a.rm_od;
+  ConvTileOrigin o;
+  o.n = t / a.rm_od;
+  o.z = oz - g.PF;
+  o.y = thi * a.rm_th - g.PT;
+  o.x = twi * a.rm_tw - g.PL;
+  return o;
+}
+
+template <int BN, bool B_TMA, bool B_MN, bool A_TMA>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
-    conv_sm100_kernel(const __grid_constant__ CUtensorMap tmW, const GemmArgs args, const ConvGeom g) {
+    conv_sm100_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                      const GemmArgs args, const ConvGeom g) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int LAG = STAGES - 1;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -102,7 +139,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], CONV_GATHER_THREADS + (B_TMA ? 1 : 0));
+      mbar_init(&full[s], A_TMA ? 1 : CONV_GATHER_THREADS + (B_TMA ? 1 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -125,6 +162,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     // ------------------------------------------------ weights via TMA
     if (B_TMA && elect_one()) {
       tma_prefetch_desc(&tmW);
+      if (A_TMA) tma_prefetch_desc(&tmX);
       uint32_t fills = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
@@ -139,7 +177,18 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           const int tap = kb / g.ncb;
           const int cb = kb - tap * g.ncb;
           uint8_t* sB = ring + s * Cfg::STAGE_BYTES + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(&full[s], Cfg::B_BYTES);
+          mbar_arrive_expect_tx(&full[s], A_TMA ? Cfg::STAGE_BYTES : Cfg::B_BYTES);
+          if (A_TMA) {
+            // Activation box {64 ch, TW, TH, 1, 1}: the output rectangle's
+            // input footprint for this tap; padding taps read zeros (OOB fill).
+            const ConvTileOrigin o = conv_tile_origin(args, g, w.mt);
+            const int kd = tap / (g.KH * g.KW);
+            const int khw = tap - kd * (g.KH * g.KW);
+            const int kh = khw / g.KW;
+            const int kw = khw - kh * g.KW;
+            tma_load_5d(&tmX, &full[s], ring + s * Cfg::STAGE_BYTES, cb * 64, o.x + kw * g.DX, o.y + kh * g.DY,
+                        o.z + kd * g.DZ, o.n);
+          }
           if (!B_MN) {
             // [Cout][taps][Cin]: box 64(Cin) x 1(tap) x BN(Cout)
             tma_load_3d(&tmW, &full[s], sB, cb * 64, tap, w.nt * BN);
@@ -159,16 +208,18 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
   } else if (warp == 1) {
     if (elect_one())
-      mma_role<BN, false, B_MN, STAGES, Cfg::STAGE_BYTES, Cfg::A_BYTES, true>(args, ring, full, empty, tmem_full,
+      mma_role<BN, false, B_MN, STAGES, Cfg::STAGE_BYTES, Cfg::A_BYTES, !A_TMA>(args, ring, full, empty, tmem_full,
                                                                            tmem_empty, drain, tmem_base, wd);
   } else if (warp < 6) {
     epilogue_role<BN, MODE_DIRECT_F16>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, wd, warp, lane);
-  } else {
+  } else if (!A_TMA) {
     // ------------------------------------------------ activation gather
     const int gt = threadIdx.x - CONV_GATHER_T0;  // 0..127
     const int j = gt & 7;                          // 16-byte channel chunk within the 128-byte row
     const int rg = gt >> 3;                        // rows rg, rg+16, ..., rg+112
     const long long m_total = static_cast<long long>(g.N) * g.OD * g.OH * g.OW;
+    // Launch-uniform: activations by 16-byte cp.async and weights by TMA.
+    const bool fast = B_TMA && g.x_vec;
     uint32_t fills = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
@@ -263,21 +314,21 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                          : "memory");
           }
         }
-        cp_async_commit();
-        if (fills >= static_cast<uint32_t>(LAG)) {
-          cp_async_wait<LAG>();
+        if (fast) {
+          // The hardware arrives once this thread's copies have landed; the
+          // MMA thread fences the async proxy after its wait.
+          cp_async_arrive_noinc(&full[s]);
+        } else {
+          // Ordinary st.shared writes (and any cp.async) complete here.
+          cp_async_wait_all();
           fence_proxy_async_smem();
-          mbar_arrive(&full[(fills - LAG) % STAGES]);
+          mbar_arrive(&full[s]);
         }
         ++fills;
       }
     }
-    // Publish the stages still in flight (also on the abort path, so no copy
-    // is left outstanding when the CTA exits).
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    const uint32_t first = fills > static_cast<uint32_t>(LAG) ? fills - LAG : 0u;
-    for (uint32_t i = first; i < fills; ++i) mbar_arrive(&full[i % STAGES]);
+    // Never leave with copies in flight (also on the abort path).
+    cp_async_wait_all();
   }
 
   tc_fence_before();

@@ -50,6 +50,12 @@ struct GemmArgs {
   float* ws;              // [num_m_tiles*128][ws_ld] fp32, split-K only
   int* counters;          // [num_tiles], split-K only
   int ws_ld;
+  int coop_finalize;      // split-K: all units co-resident (cooperative launch), slices finalized in parallel
+  // Output row map of the direct epilogue. 0: tile row r is output row
+  // mt*128 + r (GEMM). 1: a tile is a rm_th x rm_tw rectangle of output
+  // pixels of one (n, oz) plane (convolution with TMA-fed activations).
+  int rowmap;
+  int rm_tw, rm_th, rm_tiles_w, rm_tiles_h, rm_od, rm_oh, rm_ow;
   int* status;
   unsigned long long timeout_ns;
 };
@@ -63,8 +69,12 @@ struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
   static constexpr int B_BYTES = BN * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr int STAGES = (BN == 512) ? 2 : (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int ACC_BUFS = (BN == 512) ? 1 : 2;  // TMEM has 512 fp32 columns
+  static constexpr int TMEM_COLS = ACC_BUFS * BN;
+  static constexpr int N_INSTR = BN < 256 ? BN : 256;    // UMMA N per instruction
+  static constexpr int N_HALVES = BN / N_INSTR;
+  static constexpr int B_BOX_N = BN < 256 ? BN : 256;    // K-major B: TMA box rows
   // ring + barriers/slots + alignment slack
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
 };
@@ -77,6 +87,7 @@ enum : int {
   SITE_GEMM_MMA_FULL = 4,
   SITE_GEMM_MMA_DRAIN = 5,
   SITE_GEMM_EPI_TMEM_FULL = 6,
+  SITE_GEMM_EPI_TILE_RENDEZVOUS = 7,
 };
 
 struct GemmUnit {
@@ -129,14 +140,17 @@ template <int BN, bool A_MN, bool B_MN, int STAGES, int STAGE_BYTES, int A_BYTES
 __device__ __forceinline__ void mma_role(const GemmArgs& args, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                          uint64_t* tmem_full, uint64_t* tmem_empty, uint64_t* drain,
                                          uint32_t tmem_base, const Watchdog& wd) {
-  constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BM, BN, A_MN, B_MN);
+  using Cfg = GemmCfg<BN>;
+  constexpr uint32_t IDESC = idesc_f16_f32(GEMM_BM, Cfg::N_INSTR, A_MN, B_MN);
+  // Byte offset of the second N half of the B tile (BN = 512).
+  constexpr uint32_t B_HALF = B_MN ? (Cfg::N_INSTR / 64) * 8192u : Cfg::N_INSTR * 128u;
   uint32_t consumed = 0;
   uint32_t tiles_done = 0;
   bool ok = true;
   for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
     const GemmUnit w = gemm_decode_unit(args, u);
-    const uint32_t acc = tiles_done & 1u;
-    const uint32_t aph = (tiles_done >> 1) & 1u;
+    const uint32_t acc = tiles_done % Cfg::ACC_BUFS;
+    const uint32_t aph = (tiles_done / Cfg::ACC_BUFS) & 1u;
     if (!mbar_wait(&tmem_empty[acc], aph ^ 1u, wd, SITE_GEMM_MMA_TMEM_EMPTY)) break;
     tc_fence_after();
     const uint32_t d_tmem = tmem_base + acc * BN;
@@ -155,9 +169,12 @@ __device__ __forceinline__ void mma_role(const GemmArgs& args, uint8_t* ring, ui
       for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
         const uint64_t adesc =
             A_MN ? sw128_desc(a_base + kk * 2048, 8192, 1024) : sw128_desc(a_base + kk * 32, 16, 1024);
-        const uint64_t bdesc =
-            B_MN ? sw128_desc(b_base + kk * 2048, 8192, 1024) : sw128_desc(b_base + kk * 32, 16, 1024);
-        umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int hh = 0; hh < Cfg::N_HALVES; ++hh) {
+          const uint32_t bb = b_base + hh * B_HALF;
+          const uint64_t bdesc = B_MN ? sw128_desc(bb + kk * 2048, 8192, 1024) : sw128_desc(bb + kk * 32, 16, 1024);
+          umma_f16_ss(d_tmem + hh * Cfg::N_INSTR, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+        }
       }
       umma_commit(&empty[s]);
       ++consumed;
@@ -180,19 +197,34 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
                                               const Watchdog& wd, int warp, int lane) {
   constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
   constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
+  using Cfg = GemmCfg<BN>;
   const int q = warp & 3;  // TMEM lane quarter this warp may access
   const int row_in_tile = q * 32 + lane;
   const int ethread = threadIdx.x - 64;  // 0..127
   uint32_t tiles_done = 0;
   for (int u = blockIdx.x; u < args.num_units; u += gridDim.x) {
     const GemmUnit w = gemm_decode_unit(args, u);
-    const uint32_t acc = tiles_done & 1u;
-    const uint32_t aph = (tiles_done >> 1) & 1u;
+    const uint32_t acc = tiles_done % Cfg::ACC_BUFS;
+    const uint32_t aph = (tiles_done / Cfg::ACC_BUFS) & 1u;
     bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
     if (!epi_consensus(ok, q, lane, s_vote)) break;
     tc_fence_after();
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-    const int row = w.mt * GEMM_BM + row_in_tile;
+    int row = w.mt * GEMM_BM + row_in_tile;
+    bool row_ok = row < args.M;
+    if (args.rowmap == 1) {
+      int t = w.mt;
+      const int twi = t % args.rm_tiles_w;
+      t /= args.rm_tiles_w;
+      const int thi = t % args.rm_tiles_h;
+      t /= args.rm_tiles_h;
+      const int oz = t % args.rm_od;
+      const int n = t / args.rm_od;
+      const int oh = thi * args.rm_th + row_in_tile / args.rm_tw;
+      const int ow = twi * args.rm_tw + row_in_tile % args.rm_tw;
+      row_ok = oh < args.rm_oh && ow < args.rm_ow;
+      row = ((n * args.rm_od + oz) * args.rm_oh + oh) * args.rm_ow + ow;
+    }
     const int col0 = w.nt * BN;
 
 #pragma unroll 1
@@ -214,7 +246,7 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
                                 __uint_as_float(r[j + 3])));
         }
       } else if constexpr (OUT_F32) {
-        if (row < args.M) {
+        if (row_ok) {
           float* dst = args.C32 + static_cast<size_t>(row) * args.N + cbase;
           const bool vec = (cbase + 32 <= args.N) && ((args.N & 3) == 0) &&
                            ((reinterpret_cast<uintptr_t>(args.C32) & 15u) == 0);
@@ -241,7 +273,7 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
               if (cbase + j < args.N) v[j] += __half2float(args.bias[cbase + j]);
           }
         }
-        if (row < args.M) {
+        if (row_ok) {
           __half* dst = args.C + static_cast<size_t>(row) * args.N + cbase;
           const bool vec = (cbase + 32 <= args.N) && ((args.N & 7) == 0) &&
                            ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0);
@@ -265,16 +297,46 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
 
     if constexpr (SPLITK) {
       // Publish this unit's partial, then count arrivals for the tile.
+      // counters[2*tile] counts arrivals, counters[2*tile+1] departures.
       __threadfence();
       named_barrier(1, 128);
+      int* arrive_ctr = &args.counters[2 * w.tile];
+      int* depart_ctr = arrive_ctr + 1;
       if (ethread == 0) {
-        const int prev = atomicAdd(&args.counters[w.tile], 1);
-        *s_last = (prev == args.splits - 1) ? 1 : 0;
+        const int prev = atomicAdd(arrive_ctr, 1);
+        if (!args.coop_finalize) {
+          *s_last = (prev == args.splits - 1) ? 1 : 0;
+        } else {
+          // All units are co-resident (cooperative launch): wait, bounded,
+          // until every split of this tile has published its partial.
+          int ok = 1;
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t spins = 0;
+          while (*reinterpret_cast<volatile int*>(arrive_ctr) < args.splits) {
+            if ((++spins & 63u) == 0 &&
+                (aborted(wd.status) || globaltimer_ns() - t0 > wd.limit_ns)) {
+              record_error(wd.status, MM4_ERR_TIMEOUT, SITE_GEMM_EPI_TILE_RENDEZVOUS);
+              ok = 0;
+              break;
+            }
+          }
+          *s_last = ok;
+        }
       }
       named_barrier(1, 128);
+      int r_begin = 0, r_end = 0;  // tile rows this CTA finalizes
       if (*s_last) {
+        if (args.coop_finalize) {
+          const int split = u / args.num_tiles;
+          r_begin = (split * GEMM_BM) / args.splits;
+          r_end = ((split + 1) * GEMM_BM) / args.splits;
+        } else {
+          r_end = GEMM_BM;
+        }
+      }
+      if (r_end > r_begin) {
         __threadfence();
-        // Last arrival: finalize the whole tile, re-zero workspace + counter.
+        // Sum is complete: add bias, round, store; re-zero the workspace rows.
         constexpr int TPR = BN / 4;          // threads per row (float4 each)
         constexpr int RPI = 128 / TPR;       // rows per iteration
         const int tr = ethread / TPR;
@@ -288,7 +350,7 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
           if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
         }
 #pragma unroll 4
-        for (int rr = tr; rr < GEMM_BM; rr += RPI) {
+        for (int rr = r_begin + tr; rr < r_end; rr += RPI) {
           const int grow = w.mt * GEMM_BM + rr;
           float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
           const float4 s4 = __ldcg(src);
@@ -320,17 +382,36 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
             }
           }
         }
-        if (ethread == 0) args.counters[w.tile] = 0;
+      }
+      // Leave the counters at zero for the next launch.
+      if (!args.coop_finalize) {
+        if (*s_last && ethread == 0) *arrive_ctr = 0;
+      } else if (*s_last) {
+        named_barrier(1, 128);
+        if (ethread == 0) {
+          __threadfence();
+          if (atomicAdd(depart_ctr, 1) == args.splits - 1) {
+            *arrive_ctr = 0;
+            *depart_ctr = 0;
+          }
+        }
       }
     }
     ++tiles_done;
   }
 }
 
+// Split-K streams each A/B k-slab from HBM exactly once per tile, so its loads
+// are DRAM-latency bound with only STAGES slabs in shared memory. The producer
+// therefore prefetches into L2 GEMM_PF k-blocks ahead: A through a second,
+// unswizzled tensor map whose 256-wide boxes read 512 contiguous bytes per row
+// (four k-blocks), B through its regular boxes.
+constexpr int GEMM_PF = 8;
+
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmApf, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -380,11 +461,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_prefetch_desc(&tmB);
       uint32_t fills = 0;
       bool ok = true;
+      constexpr bool PREFETCH = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32) && !A_MN;
       for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
         const GemmUnit w = gemm_decode_unit(args, u);
+        // L2 prefetch of k-block t: B boxes every block, A every 4th block.
+        auto prefetch = [&](int t) {
+          if (t >= w.kb1) return;
+          if (((t - w.kb0) & 3) == 0) tma_prefetch_l2_2d(&tmApf, t * GEMM_BK, w.mt * GEMM_BM);
+          if (!B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / Cfg::B_BOX_N; ++j)
+              tma_prefetch_l2_2d(&tmB, t * GEMM_BK, w.nt * BN + j * Cfg::B_BOX_N);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, w.nt * BN + 64 * j, t * GEMM_BK);
+          }
+        };
+        if (PREFETCH)
+          for (int t = w.kb0; t < w.kb0 + GEMM_PF; ++t) prefetch(t);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           const int s = static_cast<int>(fills % STAGES);
           const uint32_t ph = (fills / STAGES) & 1u;
+          if (PREFETCH) prefetch(kb + GEMM_PF);
           if (!mbar_wait(&empty[s], ph ^ 1u, wd, SITE_GEMM_PRODUCER_EMPTY)) {
             ok = false;
             break;
@@ -400,7 +498,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tma_load_2d(&tmA, &full[s], sA + 8192, w.mt * GEMM_BM + 64, k0);
           }
           if (!B_MN) {
-            tma_load_2d(&tmB, &full[s], sB, k0, w.nt * BN);
+#pragma unroll
+            for (int j = 0; j < BN / Cfg::B_BOX_N; ++j)
+              tma_load_2d(&tmB, &full[s], sB + j * Cfg::B_BOX_N * 128, k0, w.nt * BN + j * Cfg::B_BOX_N);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(&tmB, &full[s], sB + j * 8192, w.nt * BN + 64 * j, k0);

@@ -23,6 +23,9 @@ struct mm4_conv_plan {
   int num_m_tiles, num_n_tiles;
   bool w_tma_shape;  // weight pitch allows TMA (pointer alignment checked per run)
   bool w_mn;         // HWIO / DHWIO: Cout contiguous
+  bool x_tma_shape;  // stride 1 and 16-byte channel pitch: activations by TMA
+  int tw, th;        // output rectangle per tile on the TMA path (tw * th = 128)
+  int tiles_w, tiles_h;
   char name[96];
 };
 
@@ -43,30 +46,40 @@ mm4_status finish_plan(mm4_conv_plan* p) {
   p->num_n_tiles = (g.O + p->bn - 1) / p->bn;
   p->w_mn = (g.w_layout == MM4_WEIGHTS_HWIO || g.w_layout == MM4_WEIGHTS_DHWIO);
   p->w_tma_shape = p->w_mn ? (g.O % 8 == 0) : (g.C % 8 == 0);
+  p->x_tma_shape = p->w_tma_shape && g.C % 8 == 0 && g.SX == 1 && g.SY == 1 && g.SZ == 1;
+  p->tw = g.OW > 32 ? 64 : g.OW > 16 ? 32 : g.OW > 8 ? 16 : 8;
+  p->th = GEMM_BM / p->tw;
+  p->tiles_w = (g.OW + p->tw - 1) / p->tw;
+  p->tiles_h = (g.OH + p->th - 1) / p->th;
   snprintf(p->name, sizeof(p->name), "conv_sm100<BN=%d,%s,%s>", p->bn,
            p->w_tma_shape ? (p->w_mn ? "W:tma-MN" : "W:tma-K") : "W:gather",
-           (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
+           p->x_tma_shape ? "X:tma-rect" : (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
   return MM4_OK;
 }
 
-template <int BN, bool B_TMA, bool B_MN>
-mm4_status launch(const CUtensorMap& tm, const GemmArgs& args, const ConvGeom& g, int grid, cudaStream_t st) {
-  auto kern = conv_sm100_kernel<BN, B_TMA, B_MN>;
+template <int BN, bool B_TMA, bool B_MN, bool A_TMA>
+mm4_status launch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& args, const ConvGeom& g, int grid,
+                  cudaStream_t st) {
+  auto kern = conv_sm100_kernel<BN, B_TMA, B_MN, A_TMA>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (rc != MM4_OK) return rc;
-  kern<<<grid, CONV_THREADS, smem, st>>>(tm, args, g);
+  kern<<<grid, CONV_THREADS, smem, st>>>(tw, tx, args, g);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "conv_sm100_kernel launch");
   return MM4_OK;
 }
 
 template <int BN>
-mm4_status launch_bn(bool tma, bool mn, const CUtensorMap& tm, const GemmArgs& args, const ConvGeom& g, int grid,
-                     cudaStream_t st) {
-  if (!tma) return launch<BN, false, false>(tm, args, g, grid, st);
-  if (mn) return launch<BN, true, true>(tm, args, g, grid, st);
-  return launch<BN, true, false>(tm, args, g, grid, st);
+mm4_status launch_bn(bool wtma, bool mn, bool xtma, const CUtensorMap& tw, const CUtensorMap& tx,
+                     const GemmArgs& args, const ConvGeom& g, int grid, cudaStream_t st) {
+  if (!wtma) return launch<BN, false, false, false>(tw, tx, args, g, grid, st);
+  if (xtma) {
+    if (mn) return launch<BN, true, true, true>(tw, tx, args, g, grid, st);
+    return launch<BN, true, false, true>(tw, tx, args, g, grid, st);
+  }
+  if (mn) return launch<BN, true, true, false>(tw, tx, args, g, grid, st);
+  return launch<BN, true, false, false>(tw, tx, args, g, grid, st);
 }
 
 mm4_status check_layout_2d(int layout) {
@@ -225,14 +238,38 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
     }
     if (rc != MM4_OK) return rc;
   }
+  const bool xtma = tma && p->x_tma_shape && aligned16(x);
+  CUtensorMap tx;
+  memset(&tx, 0, sizeof(tx));
+  if (xtma) {  // NDHWC activations: box {64 ch, TW, TH, 1, 1}
+    const uint64_t dims[5] = {static_cast<uint64_t>(g.C), static_cast<uint64_t>(g.W), static_cast<uint64_t>(g.H),
+                              static_cast<uint64_t>(g.D), static_cast<uint64_t>(g.N)};
+    const uint64_t strides[4] = {static_cast<uint64_t>(g.C) * 2, static_cast<uint64_t>(g.W) * g.C * 2,
+                                 static_cast<uint64_t>(g.H) * g.W * g.C * 2,
+                                 static_cast<uint64_t>(g.D) * g.H * g.W * g.C * 2};
+    const uint32_t box[5] = {64, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1, 1};
+    rc = encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != MM4_OK) return rc;
+  }
 
   GemmArgs args{};
   args.M = static_cast<int>(p->m_total);
   args.N = g.O;
   args.K = g.taps * g.C;
   args.num_m_tiles = p->num_m_tiles;
+  if (xtma) {
+    args.rowmap = 1;
+    args.rm_tw = p->tw;
+    args.rm_th = p->th;
+    args.rm_tiles_w = p->tiles_w;
+    args.rm_tiles_h = p->tiles_h;
+    args.rm_od = g.OD;
+    args.rm_oh = g.OH;
+    args.rm_ow = g.OW;
+    args.num_m_tiles = g.N * g.OD * p->tiles_h * p->tiles_w;
+  }
   args.num_n_tiles = p->num_n_tiles;
-  args.num_tiles = p->num_m_tiles * p->num_n_tiles;
+  args.num_tiles = args.num_m_tiles * p->num_n_tiles;
   args.splits = 1;
   args.kb_total = g.taps * g.ncb;
   args.num_units = args.num_tiles;
@@ -243,8 +280,8 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   args.timeout_ns = wait_timeout_ns();
   const int grid = std::min(args.num_units, info.sm_count);
   for (int i = 0; i < duplicated_count; ++i) {
-    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, tm, args, g, grid, st)
-                        : launch_bn<128>(tma, p->w_mn, tm, args, g, grid, st);
+    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, xtma, tm, tx, args, g, grid, st)
+                        : launch_bn<128>(tma, p->w_mn, xtma, tm, tx, args, g, grid, st);
     if (rc != MM4_OK) return rc;
   }
   return MM4_OK;

@@ -7,6 +7,7 @@
 // (BN x operand majors x epilogue mode) when the plan is created.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <new>
 
 #include "gemm_simt.cuh"
@@ -19,39 +20,65 @@ using namespace mm4;
 
 namespace {
 
-using GemmKernelFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
-
 template <int BN, bool AMN, bool BMN, int MODE>
-mm4_status launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+mm4_status launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf, const GemmArgs& args,
+                     int grid,
                      cudaStream_t st) {
   auto kern = gemm_sm100_kernel<BN, AMN, BMN, MODE>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (rc != MM4_OK) return rc;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, args);
+  if (args.coop_finalize) {
+    // Every work unit has its own co-resident CTA; the launch fails (rather
+    // than deadlocks) if the grid cannot be co-resident.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tapf, args);
+    if (e == cudaSuccess) return MM4_OK;
+    cudaGetLastError();
+    GemmArgs fallback = args;
+    fallback.coop_finalize = 0;
+    kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, fallback);
+  } else {
+    kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, args);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm_sm100_kernel launch");
   return MM4_OK;
 }
 
 template <int BN, bool AMN, bool BMN>
-mm4_status launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+mm4_status launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf,
+                       const GemmArgs& args, int grid,
                        cudaStream_t st) {
+  if constexpr (BN == 512) {  // BN = 512 is a split-K-only tile
+    if (mode == MODE_SPLITK_F16) return launch_tc<BN, AMN, BMN, MODE_SPLITK_F16>(ta, tb, tapf, args, grid, st);
+    return launch_tc<BN, AMN, BMN, MODE_SPLITK_F32>(ta, tb, tapf, args, grid, st);
+  }
   switch (mode) {
-    case MODE_DIRECT_F16: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F16>(ta, tb, args, grid, st);
-    case MODE_SPLITK_F16: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F16>(ta, tb, args, grid, st);
-    case MODE_DIRECT_F32: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F32>(ta, tb, args, grid, st);
-    default: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F32>(ta, tb, args, grid, st);
+    case MODE_DIRECT_F16: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F16>(ta, tb, tapf, args, grid, st);
+    case MODE_SPLITK_F16: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F16>(ta, tb, tapf, args, grid, st);
+    case MODE_DIRECT_F32: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F32>(ta, tb, tapf, args, grid, st);
+    default: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F32>(ta, tb, tapf, args, grid, st);
   }
 }
 
 template <int BN>
 mm4_status launch_bn(bool amn, bool bmn, int mode, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const CUtensorMap& tapf,
                      const GemmArgs& args, int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch_mode<BN, false, false>(mode, ta, tb, args, grid, st);
-  if (!amn && bmn) return launch_mode<BN, false, true>(mode, ta, tb, args, grid, st);
-  if (amn && !bmn) return launch_mode<BN, true, false>(mode, ta, tb, args, grid, st);
-  return launch_mode<BN, true, true>(mode, ta, tb, args, grid, st);
+  if (!amn && !bmn) return launch_mode<BN, false, false>(mode, ta, tb, tapf, args, grid, st);
+  if (!amn && bmn) return launch_mode<BN, false, true>(mode, ta, tb, tapf, args, grid, st);
+  if (amn && !bmn) return launch_mode<BN, true, false>(mode, ta, tb, tapf, args, grid, st);
+  return launch_mode<BN, true, true>(mode, ta, tb, tapf, args, grid, st);
 }
 
 // Element strides of A(m, k) and B(k, n) for the reference's transpose flags.
@@ -91,9 +118,17 @@ mm4_status run_simt(const mm4_gemm_plan* p, const void* A, const void* B, const 
   return MM4_OK;
 }
 
-mm4_status build_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUtensorMap* ta, CUtensorMap* tb) {
+mm4_status build_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUtensorMap* ta, CUtensorMap* tb,
+                      CUtensorMap* tapf) {
   const mm4_gemm_desc& d = p->d;
   mm4_status rc;
+  if (!d.transpose_left && p->splits > 1) {  // A [M][K] L2-prefetch map: box 256(K) x 128(M), unswizzled
+    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
+    const uint32_t box[2] = {256, 128};
+    rc = encode_tiled(tapf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != MM4_OK) return rc;
+  }
   if (!d.transpose_left) {  // A [M][K]: box 64(K) x 128(M)
     const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
@@ -109,7 +144,7 @@ mm4_status build_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUte
   if (d.transpose_right) {  // B [N][K]: box 64(K) x BN(N)
     const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn)};
+    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn < 256 ? p->bn : 256)};
     rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {  // B [K][N]: box 64(N) x 64(K), BN/64 per stage
     const uint64_t dims[2] = {static_cast<uint64_t>(d.N), static_cast<uint64_t>(d.K)};
@@ -129,8 +164,9 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
   rc = status_word(&status);
   if (rc != MM4_OK) return rc;
 
-  CUtensorMap ta, tb;
-  rc = build_maps(p, A, B, &ta, &tb);
+  CUtensorMap ta, tb, tapf;
+  memset(&tapf, 0, sizeof(tapf));
+  rc = build_maps(p, A, B, &ta, &tb, &tapf);
   if (rc != MM4_OK) return rc;
 
   const bool out_f32 = (C32 != nullptr);
@@ -159,6 +195,7 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
     args.ws = static_cast<float*>(ws);
     args.ws_ld = p->num_n_tiles * p->bn;
     args.counters = reinterpret_cast<int*>(static_cast<char*>(ws) + p->ws_counter_offset);
+    args.coop_finalize = (args.num_units <= info.sm_count) ? 1 : 0;
     mode = out_f32 ? MODE_SPLITK_F32 : MODE_SPLITK_F16;
   } else {
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
@@ -166,8 +203,9 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
   const int grid = std::min(args.num_units, info.sm_count);
   const bool amn = p->d.transpose_left != 0;
   const bool bmn = p->d.transpose_right == 0;
-  if (p->bn == 256) return launch_bn<256>(amn, bmn, mode, ta, tb, args, grid, st);
-  return launch_bn<128>(amn, bmn, mode, ta, tb, args, grid, st);
+  if (p->bn == 512) return launch_bn<512>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
+  if (p->bn == 256) return launch_bn<256>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
+  return launch_bn<128>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
 }
 
 mm4_status validate(const mm4_gemm_desc* d) {
@@ -200,19 +238,23 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   const bool a_ok = d.transpose_left ? (d.M % 8 == 0) : (d.K % 8 == 0);
   const bool b_ok = d.transpose_right ? (d.K % 8 == 0) : (d.N % 8 == 0);
   p->tensor_core = a_ok && b_ok;
-  p->bn = (d.N <= 128) ? 128 : 256;
+  // Split-K runs few, K-heavy units: a 128 x 512 tile (one TMEM-wide
+  // accumulator) reads each A k-slab once per 512 columns. Otherwise 128 x 256
+  // with a double-buffered accumulator, or 128 x 128 for narrow N.
   p->kb_total = (d.K + GEMM_BK - 1) / GEMM_BK;
+  p->splits = std::max(1, std::min(d.split_k, p->kb_total));
+  if (!p->tensor_core) p->splits = 1;
+  p->bn = (d.N <= 128) ? 128 : 256;
+  if (p->splits > 1 && d.N > 256) p->bn = 512;
   p->num_m_tiles = (d.M + GEMM_BM - 1) / GEMM_BM;
   p->num_n_tiles = (d.N + p->bn - 1) / p->bn;
   p->num_tiles = p->num_m_tiles * p->num_n_tiles;
-  p->splits = std::max(1, std::min(d.split_k, p->kb_total));
-  if (!p->tensor_core) p->splits = 1;
   p->ws_bytes = 0;
   p->ws_counter_offset = 0;
   if (p->splits > 1) {
     const size_t acc = static_cast<size_t>(p->num_m_tiles) * GEMM_BM * p->num_n_tiles * p->bn * sizeof(float);
     p->ws_counter_offset = acc;
-    p->ws_bytes = (acc + static_cast<size_t>(p->num_tiles) * sizeof(int) + 255) & ~static_cast<size_t>(255);
+    p->ws_bytes = (acc + static_cast<size_t>(p->num_tiles) * 2 * sizeof(int) + 255) & ~static_cast<size_t>(255);
   }
   if (p->tensor_core)
     snprintf(p->name, sizeof(p->name), "gemm_sm100<BN=%d,%s%s,%s>", p->bn, d.transpose_left ? "A:MN" : "A:K",

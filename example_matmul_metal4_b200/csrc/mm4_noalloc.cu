@@ -74,30 +74,39 @@ mm4_status setup_device(int dev, void** scratch, int** status) {
 }
 
 template <int BN, bool AMN, bool BMN>
-mm4_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid, cudaStream_t st) {
+mm4_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf, const GemmArgs& args, int grid,
+                  cudaStream_t st) {
   auto kern = gemm_sm100_kernel<BN, AMN, BMN, MODE_SPLITK_F16>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (rc != MM4_OK) return rc;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, args);
+  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm_sm100_kernel (no-alloc) launch");
   return MM4_OK;
 }
 
 template <int BN>
-mm4_status launch_bn(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+mm4_status launch_bn(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf,
+                     const GemmArgs& args,
                      int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch<BN, false, false>(ta, tb, args, grid, st);
-  if (!amn && bmn) return launch<BN, false, true>(ta, tb, args, grid, st);
-  if (amn && !bmn) return launch<BN, true, false>(ta, tb, args, grid, st);
-  return launch<BN, true, true>(ta, tb, args, grid, st);
+  if (!amn && !bmn) return launch<BN, false, false>(ta, tb, tapf, args, grid, st);
+  if (!amn && bmn) return launch<BN, false, true>(ta, tb, tapf, args, grid, st);
+  if (amn && !bmn) return launch<BN, true, false>(ta, tb, tapf, args, grid, st);
+  return launch<BN, true, true>(ta, tb, tapf, args, grid, st);
 }
 
 mm4_status encode_operand_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUtensorMap* ta,
-                               CUtensorMap* tb) {
+                               CUtensorMap* tb, CUtensorMap* tapf) {
   const mm4_gemm_desc& d = p->d;
   mm4_status rc;
+  if (!d.transpose_left) {  // A L2-prefetch map: box 256(K) x 128(M), unswizzled
+    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
+    const uint32_t box[2] = {256, 128};
+    rc = encode_tiled(tapf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != MM4_OK) return rc;
+  }
   if (!d.transpose_left) {
     const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
     const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
@@ -113,7 +122,7 @@ mm4_status encode_operand_maps(const mm4_gemm_plan* p, const void* A, const void
   if (d.transpose_right) {
     const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.N)};
     const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn)};
+    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn < 256 ? p->bn : 256)};
     rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   } else {
     const uint64_t dims[2] = {static_cast<uint64_t>(d.N), static_cast<uint64_t>(d.K)};
@@ -159,8 +168,9 @@ mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* p, const void* A, co
   cudaError_t e = cudaMemsetAsync(scratch, 0, p->ws_bytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc scratch)");
 
-  CUtensorMap ta, tb;
-  rc = encode_operand_maps(p, A, B, &ta, &tb);
+  CUtensorMap ta, tb, tapf;
+  memset(&tapf, 0, sizeof(tapf));
+  rc = encode_operand_maps(p, A, B, &ta, &tb, &tapf);
   if (rc != MM4_OK) return rc;
 
   GemmArgs args{};
@@ -185,8 +195,9 @@ mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* p, const void* A, co
   const int grid = std::min(args.num_units, info.sm_count);
   const bool amn = p->d.transpose_left != 0;
   const bool bmn = p->d.transpose_right == 0;
-  if (p->bn == 256) return launch_bn<256>(amn, bmn, ta, tb, args, grid, st);
-  return launch_bn<128>(amn, bmn, ta, tb, args, grid, st);
+  if (p->bn == 512) return launch_bn<512>(amn, bmn, ta, tb, tapf, args, grid, st);
+  if (p->bn == 256) return launch_bn<256>(amn, bmn, ta, tb, tapf, args, grid, st);
+  return launch_bn<128>(amn, bmn, ta, tb, tapf, args, grid, st);
 }
 
 }  // extern "C"

@@ -71,6 +71,18 @@ def test_split_k(cuda, K, split):
     assert_close(got, ref, f"split {split} K={K}")
 
 
+@pytest.mark.parametrize("M,N,K,split,tr", [(1024, 1024, 8192, 16, False), (640, 768, 4096, 12, True),
+                                            (512, 300, 2048, 4, False), (384, 136, 4096, 8, False)])
+def test_split_k_tiles_and_finalize_modes(cuda, M, N, K, split, tr):
+    """128x512 tiles with more units than SMs (last-arriving-unit finalize),
+    with as many units as SMs or fewer (cooperative sliced finalize), N tails,
+    and both B layouts."""
+    plan, got, ref = _run(cuda, M, N, K, False, tr, split=split, rows=(0, min(M, 256)))
+    assert_close(got, ref, f"{M}x{N}x{K} split {split} {plan.kernel_name}")
+    plan, got2, ref2 = _run(cuda, M, N, K, False, tr, split=split, rows=(max(0, M - 64), M))
+    assert_close(got2, ref2, "last rows")
+
+
 def test_split_k_repeat_leaves_workspace_clean(cuda):
     """duplicatedCount re-runs the same launch; each run must re-zero its
     workspace so every repetition produces the same result."""
