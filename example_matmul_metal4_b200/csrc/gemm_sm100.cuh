@@ -18,7 +18,8 @@
 // fp32 partial into an L2-resident fp32 workspace with vector atomics, then
 // bumps a per-tile arrival counter; the unit that arrives last reads the
 // summed tile back, adds bias, writes the output and re-zeroes the workspace
-// and counter, so the workspace is clean for the next launch. The fp32
+// and counter, so the workspace is clean for the next launch. The vector
+// reductions are fire-and-forget (red.global.add.v4.f32). The fp32
 // partials never round-trip through fp16 (the reference keeps fp16 partials,
 // matmul.swift:248, :298-311), and the K tail is applied exactly once (the
 // reference applies it in every split, matmul.swift:266-277).
@@ -191,26 +192,34 @@ __device__ __forceinline__ void mma_role(const GemmArgs& args, uint8_t* ring, ui
 // ---------------------------------------------------------------------------
 // Epilogue role (warps 2-5 of the CTA, 128 threads: thread 64 + i).
 // ---------------------------------------------------------------------------
-template <int BN, int MODE>
+// PAIR: the CTA is one half (rank 0 = leader, 1 = peer) of a 2-CTA cluster
+// computing 256-row tiles with cta_group::2; its accumulator holds rows
+// rank*128..+127 of the tile, and it hands TMEM back to the leader's MMA
+// thread through the leader's tmem_empty barrier.
+template <int BN, int MODE, bool PAIR = false>
 __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tmem_full, uint64_t* tmem_empty,
                                               uint32_t tmem_base, volatile int* s_vote, volatile int* s_last,
-                                              const Watchdog& wd, int warp, int lane) {
+                                              const Watchdog& wd, int warp, int lane, uint32_t rank = 0) {
   constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
   constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
-  using Cfg = GemmCfg<BN>;
+  constexpr int ACC_BUFS = (BN == 512) ? 1 : 2;
+  constexpr int TILE_M = PAIR ? 2 * GEMM_BM : GEMM_BM;
   const int q = warp & 3;  // TMEM lane quarter this warp may access
   const int row_in_tile = q * 32 + lane;
   const int ethread = threadIdx.x - 64;  // 0..127
+  const int u0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ustep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   uint32_t tiles_done = 0;
-  for (int u = blockIdx.x; u < args.num_units; u += gridDim.x) {
+  for (int u = u0; u < args.num_units; u += ustep) {
     const GemmUnit w = gemm_decode_unit(args, u);
-    const uint32_t acc = tiles_done % Cfg::ACC_BUFS;
-    const uint32_t aph = (tiles_done / Cfg::ACC_BUFS) & 1u;
+    const uint32_t acc = tiles_done % ACC_BUFS;
+    const uint32_t aph = (tiles_done / ACC_BUFS) & 1u;
     bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
     if (!epi_consensus(ok, q, lane, s_vote)) break;
     tc_fence_after();
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-    int row = w.mt * GEMM_BM + row_in_tile;
+    const int row_base = w.mt * TILE_M + static_cast<int>(rank) * GEMM_BM;  // this CTA's first tile row
+    int row = row_base + row_in_tile;
     bool row_ok = row < args.M;
     if (args.rowmap == 1) {
       int t = w.mt;
@@ -234,16 +243,18 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       tmem_ld_wait();
       if (c == BN / 32 - 1) {
         tc_fence_before();
-        mbar_arrive(&tmem_empty[acc]);
+        if (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
+        else
+          mbar_arrive(&tmem_empty[acc]);
       }
       const int cbase = col0 + c * 32;
       if constexpr (SPLITK) {
         float* dst = args.ws + static_cast<size_t>(row) * args.ws_ld + cbase;
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          atomicAdd(reinterpret_cast<float4*>(dst + j),
-                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                __uint_as_float(r[j + 3])));
+          red_add_v4_f32(dst + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                         __uint_as_float(r[j + 3]));
         }
       } else if constexpr (OUT_F32) {
         if (row_ok) {
@@ -300,7 +311,8 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       // counters[2*tile] counts arrivals, counters[2*tile+1] departures.
       __threadfence();
       named_barrier(1, 128);
-      int* arrive_ctr = &args.counters[2 * w.tile];
+      const int ctr_tile = PAIR ? 2 * w.tile + static_cast<int>(rank) : w.tile;  // per 128-row half
+      int* arrive_ctr = &args.counters[2 * ctr_tile];
       int* depart_ctr = arrive_ctr + 1;
       if (ethread == 0) {
         const int prev = atomicAdd(arrive_ctr, 1);
@@ -351,7 +363,7 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
         }
 #pragma unroll 4
         for (int rr = r_begin + tr; rr < r_end; rr += RPI) {
-          const int grow = w.mt * GEMM_BM + rr;
+          const int grow = row_base + rr;
           float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
           const float4 s4 = __ldcg(src);
           __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
@@ -401,17 +413,10 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
   }
 }
 
-// Split-K streams each A/B k-slab from HBM exactly once per tile, so its loads
-// are DRAM-latency bound with only STAGES slabs in shared memory. The producer
-// therefore prefetches into L2 GEMM_PF k-blocks ahead: A through a second,
-// unswizzled tensor map whose 256-wide boxes read 512 contiguous bytes per row
-// (four k-blocks), B through its regular boxes.
-constexpr int GEMM_PF = 8;
-
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmApf, const GemmArgs args) {
+                      const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -461,28 +466,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tma_prefetch_desc(&tmB);
       uint32_t fills = 0;
       bool ok = true;
-      constexpr bool PREFETCH = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32) && !A_MN;
       for (int u = blockIdx.x; u < args.num_units && ok; u += gridDim.x) {
         const GemmUnit w = gemm_decode_unit(args, u);
-        // L2 prefetch of k-block t: B boxes every block, A every 4th block.
-        auto prefetch = [&](int t) {
-          if (t >= w.kb1) return;
-          if (((t - w.kb0) & 3) == 0) tma_prefetch_l2_2d(&tmApf, t * GEMM_BK, w.mt * GEMM_BM);
-          if (!B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / Cfg::B_BOX_N; ++j)
-              tma_prefetch_l2_2d(&tmB, t * GEMM_BK, w.nt * BN + j * Cfg::B_BOX_N);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_2d(&tmB, w.nt * BN + 64 * j, t * GEMM_BK);
-          }
-        };
-        if (PREFETCH)
-          for (int t = w.kb0; t < w.kb0 + GEMM_PF; ++t) prefetch(t);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           const int s = static_cast<int>(fills % STAGES);
           const uint32_t ph = (fills / STAGES) & 1u;
-          if (PREFETCH) prefetch(kb + GEMM_PF);
           if (!mbar_wait(&empty[s], ph ^ 1u, wd, SITE_GEMM_PRODUCER_EMPTY)) {
             ok = false;
             break;

@@ -10,76 +10,13 @@
 #include <cstring>
 #include <new>
 
+#include "gemm_launch.cuh"
 #include "gemm_simt.cuh"
-#include "gemm_sm100.cuh"
-#include "mm4_gemm_plan.h"
-#include "mm4_internal.h"
 
 using namespace mm4;
 
 
 namespace {
-
-template <int BN, bool AMN, bool BMN, int MODE>
-mm4_status launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf, const GemmArgs& args,
-                     int grid,
-                     cudaStream_t st) {
-  auto kern = gemm_sm100_kernel<BN, AMN, BMN, MODE>;
-  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
-  mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
-  if (rc != MM4_OK) return rc;
-  if (args.coop_finalize) {
-    // Every work unit has its own co-resident CTA; the launch fails (rather
-    // than deadlocks) if the grid cannot be co-resident.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(GEMM_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tapf, args);
-    if (e == cudaSuccess) return MM4_OK;
-    cudaGetLastError();
-    GemmArgs fallback = args;
-    fallback.coop_finalize = 0;
-    kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, fallback);
-  } else {
-    kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, args);
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gemm_sm100_kernel launch");
-  return MM4_OK;
-}
-
-template <int BN, bool AMN, bool BMN>
-mm4_status launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf,
-                       const GemmArgs& args, int grid,
-                       cudaStream_t st) {
-  if constexpr (BN == 512) {  // BN = 512 is a split-K-only tile
-    if (mode == MODE_SPLITK_F16) return launch_tc<BN, AMN, BMN, MODE_SPLITK_F16>(ta, tb, tapf, args, grid, st);
-    return launch_tc<BN, AMN, BMN, MODE_SPLITK_F32>(ta, tb, tapf, args, grid, st);
-  }
-  switch (mode) {
-    case MODE_DIRECT_F16: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F16>(ta, tb, tapf, args, grid, st);
-    case MODE_SPLITK_F16: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F16>(ta, tb, tapf, args, grid, st);
-    case MODE_DIRECT_F32: return launch_tc<BN, AMN, BMN, MODE_DIRECT_F32>(ta, tb, tapf, args, grid, st);
-    default: return launch_tc<BN, AMN, BMN, MODE_SPLITK_F32>(ta, tb, tapf, args, grid, st);
-  }
-}
-
-template <int BN>
-mm4_status launch_bn(bool amn, bool bmn, int mode, const CUtensorMap& ta, const CUtensorMap& tb,
-                     const CUtensorMap& tapf,
-                     const GemmArgs& args, int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch_mode<BN, false, false>(mode, ta, tb, tapf, args, grid, st);
-  if (!amn && bmn) return launch_mode<BN, false, true>(mode, ta, tb, tapf, args, grid, st);
-  if (amn && !bmn) return launch_mode<BN, true, false>(mode, ta, tb, tapf, args, grid, st);
-  return launch_mode<BN, true, true>(mode, ta, tb, tapf, args, grid, st);
-}
 
 // Element strides of A(m, k) and B(k, n) for the reference's transpose flags.
 void operand_strides(const mm4_gemm_desc& d, long long* a_sm, long long* a_sk, long long* b_sk, long long* b_sn) {
@@ -118,43 +55,6 @@ mm4_status run_simt(const mm4_gemm_plan* p, const void* A, const void* B, const 
   return MM4_OK;
 }
 
-mm4_status build_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUtensorMap* ta, CUtensorMap* tb,
-                      CUtensorMap* tapf) {
-  const mm4_gemm_desc& d = p->d;
-  mm4_status rc;
-  if (!d.transpose_left && p->splits > 1) {  // A [M][K] L2-prefetch map: box 256(K) x 128(M), unswizzled
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {256, 128};
-    rc = encode_tiled(tapf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != MM4_OK) return rc;
-  }
-  if (!d.transpose_left) {  // A [M][K]: box 64(K) x 128(M)
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, 128};
-    rc = encode_tiled(ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  } else {  // A [K][M]: box 64(M) x 64(K), two per stage
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.M), static_cast<uint64_t>(d.K)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.M) * 2};
-    const uint32_t box[2] = {64, 64};
-    rc = encode_tiled(ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  }
-  if (rc != MM4_OK) return rc;
-  if (d.transpose_right) {  // B [N][K]: box 64(K) x BN(N)
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.N)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn < 256 ? p->bn : 256)};
-    rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  } else {  // B [K][N]: box 64(N) x 64(K), BN/64 per stage
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.N), static_cast<uint64_t>(d.K)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.N) * 2};
-    const uint32_t box[2] = {64, 64};
-    rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  }
-  return rc;
-}
-
 mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const void* bias, void* C, float* C32,
                   void* ws, size_t ws_bytes, cudaStream_t st) {
   DeviceInfo info;
@@ -164,23 +64,13 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
   rc = status_word(&status);
   if (rc != MM4_OK) return rc;
 
-  CUtensorMap ta, tb, tapf;
-  memset(&tapf, 0, sizeof(tapf));
-  rc = build_maps(p, A, B, &ta, &tb, &tapf);
+  CUtensorMap ta, tb;
+  rc = gemm_build_maps(p, A, B, &ta, &tb);
   if (rc != MM4_OK) return rc;
 
   const bool out_f32 = (C32 != nullptr);
   GemmArgs args{};
-  args.M = p->d.M;
-  args.N = p->d.N;
-  args.K = p->d.K;
-  args.num_m_tiles = p->num_m_tiles;
-  args.num_n_tiles = p->num_n_tiles;
-  args.num_tiles = p->num_tiles;
-  args.splits = p->splits;
-  args.kb_total = p->kb_total;
-  args.num_units = p->num_tiles * p->splits;
-  args.group_m = 8;
+  gemm_plan_args(p, &args);
   args.bias = out_f32 ? nullptr : static_cast<const __half*>(bias);
   args.C = static_cast<__half*>(C);
   args.C32 = C32;
@@ -193,19 +83,14 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
       return fail(MM4_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, p->ws_bytes);
     if (!aligned16(ws)) return fail(MM4_ERR_WORKSPACE, "workspace must be 16-byte aligned");
     args.ws = static_cast<float*>(ws);
-    args.ws_ld = p->num_n_tiles * p->bn;
     args.counters = reinterpret_cast<int*>(static_cast<char*>(ws) + p->ws_counter_offset);
-    args.coop_finalize = (args.num_units <= info.sm_count) ? 1 : 0;
+    const int ctas = p->pair ? 2 * args.num_units : args.num_units;
+    args.coop_finalize = (ctas <= info.sm_count) ? 1 : 0;
     mode = out_f32 ? MODE_SPLITK_F32 : MODE_SPLITK_F16;
   } else {
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
   }
-  const int grid = std::min(args.num_units, info.sm_count);
-  const bool amn = p->d.transpose_left != 0;
-  const bool bmn = p->d.transpose_right == 0;
-  if (p->bn == 512) return launch_bn<512>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
-  if (p->bn == 256) return launch_bn<256>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
-  return launch_bn<128>(amn, bmn, mode, ta, tb, tapf, args, grid, st);
+  return gemm_dispatch(p, mode, ta, tb, args, gemm_grid(p, args.num_units, info.sm_count), st);
 }
 
 mm4_status validate(const mm4_gemm_desc* d) {
@@ -244,20 +129,30 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   p->kb_total = (d.K + GEMM_BK - 1) / GEMM_BK;
   p->splits = std::max(1, std::min(d.split_k, p->kb_total));
   if (!p->tensor_core) p->splits = 1;
+  // Tile choice. CTA pairs (cta_group::2, 256-row tiles, each CTA staging half
+  // of B) when M and N are both at least 256; split-K then uses 256 x 512 pair
+  // tiles (one TMEM-wide accumulator per CTA) so each A k-slab is read once
+  // per 512 columns. Otherwise one CTA with 128 x 256 (or 128 x 128 for
+  // narrow N; 128 x 512 for wide split-K).
+  p->pair = p->tensor_core && d.M >= 256 && d.N >= 256;
   p->bn = (d.N <= 128) ? 128 : 256;
   if (p->splits > 1 && d.N > 256) p->bn = 512;
-  p->num_m_tiles = (d.M + GEMM_BM - 1) / GEMM_BM;
+  p->num_m_tiles = (d.M + (p->pair ? 2 * GEMM_BM : GEMM_BM) - 1) / (p->pair ? 2 * GEMM_BM : GEMM_BM);
   p->num_n_tiles = (d.N + p->bn - 1) / p->bn;
   p->num_tiles = p->num_m_tiles * p->num_n_tiles;
   p->ws_bytes = 0;
   p->ws_counter_offset = 0;
   if (p->splits > 1) {
-    const size_t acc = static_cast<size_t>(p->num_m_tiles) * GEMM_BM * p->num_n_tiles * p->bn * sizeof(float);
+    const int tile_m = p->pair ? 2 * GEMM_BM : GEMM_BM;
+    const size_t acc = static_cast<size_t>(p->num_m_tiles) * tile_m * p->num_n_tiles * p->bn * sizeof(float);
     p->ws_counter_offset = acc;
-    p->ws_bytes = (acc + static_cast<size_t>(p->num_tiles) * 2 * sizeof(int) + 255) & ~static_cast<size_t>(255);
+    // two counters (arrivals, departures) per 128-row half tile
+    const size_t counters = static_cast<size_t>(p->num_tiles) * (p->pair ? 2 : 1) * 2 * sizeof(int);
+    p->ws_bytes = (acc + counters + 255) & ~static_cast<size_t>(255);
   }
   if (p->tensor_core)
-    snprintf(p->name, sizeof(p->name), "gemm_sm100<BN=%d,%s%s,%s>", p->bn, d.transpose_left ? "A:MN" : "A:K",
+    snprintf(p->name, sizeof(p->name), "gemm_sm100%s<BM=%d,BN=%d,%s%s,%s>", p->pair ? "_pair" : "",
+             p->pair ? 2 * GEMM_BM : GEMM_BM, p->bn, d.transpose_left ? "A:MN" : "A:K",
              d.transpose_right ? ",B:K" : ",B:MN", p->splits > 1 ? "splitk" : "direct");
   else
     snprintf(p->name, sizeof(p->name), "gemm_simt<unaligned>");

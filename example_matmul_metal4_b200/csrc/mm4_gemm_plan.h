@@ -8,7 +8,8 @@
 struct mm4_gemm_plan {
   mm4_gemm_desc d;
   bool tensor_core;  // false: reduced-alignment SIMT kernel
-  int bn;
+  bool pair;         // 2-CTA cluster kernel (cta_group::2), 256-row tiles
+  int bn;            // tile N (per CTA for one-CTA tiles, per pair otherwise)
   int splits;
   int kb_total;
   int num_m_tiles, num_n_tiles, num_tiles;

@@ -33,9 +33,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "gemm_sm100.cuh"
-#include "mm4_gemm_plan.h"
-#include "mm4_internal.h"
+#include "gemm_launch.cuh"
 
 using namespace mm4;
 
@@ -73,66 +71,6 @@ mm4_status setup_device(int dev, void** scratch, int** status) {
   return MM4_OK;
 }
 
-template <int BN, bool AMN, bool BMN>
-mm4_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf, const GemmArgs& args, int grid,
-                  cudaStream_t st) {
-  auto kern = gemm_sm100_kernel<BN, AMN, BMN, MODE_SPLITK_F16>;
-  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
-  mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
-  if (rc != MM4_OK) return rc;
-  kern<<<grid, GEMM_THREADS, smem, st>>>(ta, tb, tapf, args);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "gemm_sm100_kernel (no-alloc) launch");
-  return MM4_OK;
-}
-
-template <int BN>
-mm4_status launch_bn(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tapf,
-                     const GemmArgs& args,
-                     int grid, cudaStream_t st) {
-  if (!amn && !bmn) return launch<BN, false, false>(ta, tb, tapf, args, grid, st);
-  if (!amn && bmn) return launch<BN, false, true>(ta, tb, tapf, args, grid, st);
-  if (amn && !bmn) return launch<BN, true, false>(ta, tb, tapf, args, grid, st);
-  return launch<BN, true, true>(ta, tb, tapf, args, grid, st);
-}
-
-mm4_status encode_operand_maps(const mm4_gemm_plan* p, const void* A, const void* B, CUtensorMap* ta,
-                               CUtensorMap* tb, CUtensorMap* tapf) {
-  const mm4_gemm_desc& d = p->d;
-  mm4_status rc;
-  if (!d.transpose_left) {  // A L2-prefetch map: box 256(K) x 128(M), unswizzled
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {256, 128};
-    rc = encode_tiled(tapf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc != MM4_OK) return rc;
-  }
-  if (!d.transpose_left) {
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.M)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, 128};
-    rc = encode_tiled(ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  } else {
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.M), static_cast<uint64_t>(d.K)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.M) * 2};
-    const uint32_t box[2] = {64, 64};
-    rc = encode_tiled(ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, A, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  }
-  if (rc != MM4_OK) return rc;
-  if (d.transpose_right) {
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.K), static_cast<uint64_t>(d.N)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.K) * 2};
-    const uint32_t box[2] = {64, static_cast<uint32_t>(p->bn < 256 ? p->bn : 256)};
-    rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  } else {
-    const uint64_t dims[2] = {static_cast<uint64_t>(d.N), static_cast<uint64_t>(d.K)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(d.N) * 2};
-    const uint32_t box[2] = {64, 64};
-    rc = encode_tiled(tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  }
-  return rc;
-}
-
 }  // namespace
 
 extern "C" {
@@ -168,36 +106,21 @@ mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* p, const void* A, co
   cudaError_t e = cudaMemsetAsync(scratch, 0, p->ws_bytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc scratch)");
 
-  CUtensorMap ta, tb, tapf;
-  memset(&tapf, 0, sizeof(tapf));
-  rc = encode_operand_maps(p, A, B, &ta, &tb, &tapf);
+  CUtensorMap ta, tb;
+  rc = gemm_build_maps(p, A, B, &ta, &tb);
   if (rc != MM4_OK) return rc;
 
   GemmArgs args{};
-  args.M = p->d.M;
-  args.N = p->d.N;
-  args.K = p->d.K;
-  args.num_m_tiles = p->num_m_tiles;
-  args.num_n_tiles = p->num_n_tiles;
-  args.num_tiles = p->num_tiles;
-  args.splits = p->splits;
-  args.kb_total = p->kb_total;
-  args.num_units = p->num_tiles * p->splits;
-  args.group_m = 8;
+  gemm_plan_args(p, &args);
   args.bias = static_cast<const __half*>(bias);
   args.C = static_cast<__half*>(C);
   args.C32 = nullptr;
   args.ws = static_cast<float*>(scratch);
-  args.ws_ld = p->num_n_tiles * p->bn;
   args.counters = reinterpret_cast<int*>(static_cast<char*>(scratch) + p->ws_counter_offset);
+  args.coop_finalize = 0;  // the last-arriving unit of each tile finalizes it
   args.status = status;
   args.timeout_ns = wait_timeout_ns();
-  const int grid = std::min(args.num_units, info.sm_count);
-  const bool amn = p->d.transpose_left != 0;
-  const bool bmn = p->d.transpose_right == 0;
-  if (p->bn == 512) return launch_bn<512>(amn, bmn, ta, tb, tapf, args, grid, st);
-  if (p->bn == 256) return launch_bn<256>(amn, bmn, ta, tb, tapf, args, grid, st);
-  return launch_bn<128>(amn, bmn, ta, tb, tapf, args, grid, st);
+  return gemm_dispatch(p, MODE_SPLITK_F16, ta, tb, args, gemm_grid(p, args.num_units, info.sm_count), st);
 }
 
 }  // extern "C"
