@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const GemmUnit w = gemm_decode_unit(args, u);
         const uint32_t acc = tiles_done % Cfg::ACC_BUFS;
         const uint32_t aph = (tiles_done / Cfg::ACC_BUFS) & 1u;
-        if (!mbar_wait(&tmem_empty[acc], aph ^ 1u, wd, SITE_PAIR_MMA_TMEM_EMPTY)) break;
+        if (!mbar_wait_cluster(&tmem_empty[acc], aph ^ 1u, wd, SITE_PAIR_MMA_TMEM_EMPTY)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
