@@ -6,23 +6,29 @@
 // one multiply, as attention.swift:24 folds it into dotScale), fp16 P, fp32 O,
 // and a final O * (1/l) epilogue (:354-379).
 //
-// One CTA per (batch, head, 128-row query tile); head_dim D = 128. 8 warps:
-//   warp 0     TMA producer: Q once, then K_j / V_j (128 keys each) into
-//              two-stage rings (128-byte-swizzled boxes of 64 x 128).
-//   warp 1     TMEM alloc; one elected lane issues tcgen05.mma:
-//                S_j = Q K_j^T  (M=128, N=128, K=D) into TMEM S[j%2]
-//                O  += P_j V_j  (M=128, N=D,  K=128; V is an MN-major operand)
-//              issuing S_{j+1} before O += P_j V_j so QK^T of the next tile
-//              overlaps the softmax of the current one.
-//   warps 4-7  softmax: thread r owns query row r (TMEM lane r). Per tile it
-//              reads its S row (tcgen05.ld), takes the row max in the log2
-//              domain, and only when the max grew by more than 8 (a factor of
-//              256) rescales its O row in TMEM and its running sum l (lazy
-//              rescaling: the stale max cancels in O / l exactly). It then
-//              writes P = 2^(s - m) as fp16 into one of two swizzled smem P
-//              tiles for the P V MMA; with two P buffers the softmax of tile
-//              j+1 waits for P_j V_j only when it has to rescale O.
-//              At the end it reads O, multiplies by 1/l and stores fp16.
+// One CTA per (batch, head, 256 query rows) = two 128-row Q tiles that share
+// every K_j / V_j tile staged in shared memory; head_dim D = 128. 12 warps:
+//   warp 0      TMA producer: Q0, Q1 once, then K_j / V_j (128 keys each) into
+//               rings (128-byte-swizzled boxes of 64 x 128).
+//   warp 1      TMEM alloc (512 columns: S0 | S1 | O0 | O1); one elected lane
+//               issues tcgen05.mma in the order
+//                 S0_0 S1_0 | PV0_0 S0_1 PV1_0 S1_1 | PV0_1 S0_2 ...
+//               S_i = Q_i K_j^T (M=128, N=128, K=D, both operands in smem);
+//               O_i += P_i V_j (M=128, N=D, K=128) with P_i read from TMEM
+//               (it overwrites S_i in place) and V an MN-major smem operand.
+//               While one tile's softmax runs the tensor core works on the
+//               other tile.
+//   warps 4-7   softmax of Q tile 0, warps 8-11 of Q tile 1: thread r owns
+//               query row r (TMEM lane r). Per key tile it reads its S row
+//               (tcgen05.ld), takes the row max, and only when the max grew by
+//               more than 8 in the log2 domain (a factor of 256) rescales its O
+//               row in TMEM and its running sum l (lazy rescaling: the stale
+//               max cancels in O / l exactly). It writes P = 2^(s - m) as fp16
+//               pairs back over its S row (tcgen05.st). At the end it reads O,
+//               multiplies by 1/l and stores fp16.
+// The commit that publishes S_i(j) also covers O_i += P_i(j-1) V_{j-1} (the
+// MMAs of one thread complete in issue order), so the softmax may rescale O
+// as soon as it sees S.
 // Keys past the sequence end are masked to -inf; query rows past the end are
 // computed on zero-filled Q and not stored.
 #pragma once
@@ -41,23 +47,36 @@ struct AttnArgs {
 };
 
 constexpr int ATT_D = 128;
-constexpr int ATT_BM = 128;  // query rows per CTA
-constexpr int ATT_BN = 128;  // keys per tile
-constexpr int ATT_THREADS = 256;
-constexpr int ATT_TILE_BYTES = 128 * 128 * 2;  // 32 KB: Q, K_j, V_j or P tile
-constexpr int ATT_SMEM_BYTES = 7 * ATT_TILE_BYTES + 256 + 1024;  // Q, K[2], V[2], P[2]
+constexpr int ATT_BM = 128;                     // query rows per Q tile
+constexpr int ATT_QTILES = 2;                   // Q tiles per CTA
+constexpr int ATT_CTA_ROWS = ATT_BM * ATT_QTILES;
+constexpr int ATT_BN = 128;                     // keys per tile
+constexpr int ATT_THREADS = 384;
+constexpr int ATT_TILE_BYTES = 128 * 128 * 2;   // 32 KB: one Q, K_j or V_j tile
+#ifndef ATT_K_STAGES
+#define ATT_K_STAGES 3
+#endif
+#ifndef ATT_V_STAGES
+#define ATT_V_STAGES 2
+#endif
+// Register split: warps 0-3 (producer, MMA, two idle) give registers to the
+// two softmax warpgroups. 128 * ATT_REGS_LOW + 256 * ATT_REGS_HIGH must not
+// exceed 384 * (registers per thread at launch); the launcher checks it.
+constexpr int ATT_REGS_LOW = 96;
+constexpr int ATT_REGS_HIGH = 200;
+constexpr int ATT_REGS_NEEDED = (128 * ATT_REGS_LOW + 256 * ATT_REGS_HIGH + ATT_THREADS - 1) / ATT_THREADS;
+constexpr int ATT_SMEM_BYTES = (ATT_QTILES + ATT_K_STAGES + ATT_V_STAGES) * ATT_TILE_BYTES + 256 + 1024;
 
 enum : int {
   SITE_ATT_PRODUCER = 40,
   SITE_ATT_PRODUCER_DRAIN = 41,
   SITE_ATT_MMA_Q = 42,
   SITE_ATT_MMA_K = 43,
-  SITE_ATT_MMA_SFREE = 44,
   SITE_ATT_MMA_P = 45,
   SITE_ATT_MMA_V = 46,
   SITE_ATT_MMA_DRAIN = 47,
   SITE_ATT_SOFTMAX_S = 48,
-  SITE_ATT_SOFTMAX_PV = 49,
+  SITE_ATT_SOFTMAX_O = 49,
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -72,20 +91,26 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // iteratively reweighted least squares on [-1/2, 1/2] (max relative error
 // 7.5e-5, below fp16's half-ulp 4.9e-4: P is stored as fp16); 2^n is added
 // into the exponent field. x is clamped at -125 so the result stays a normal
-// float (masked scores become ~2e-38).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.0f);
+// float (masked scores become ~2e-38). Two lanes at a time on the packed
+// fp32x2 pipe.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
   const float kRound = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + kRound;
-  const float n = t - kRound;
-  const float f = x - n;
-  const float p = fmaf(fmaf(fmaf(0.05517161f, f, 0.24261114f), f, 0.69326103f), f, 0.99992806f);
-  const int ni = __float_as_int(t) - __float_as_int(kRound);
-  return __int_as_float(__float_as_int(p) + (ni << 23));
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = fadd2(x, make_float2(-n.x, -n.y));
+  float2 p = ffma2(make_float2(0.05517161f, 0.05517161f), f, make_float2(0.24261114f, 0.24261114f));
+  p = ffma2(p, f, make_float2(0.69326103f, 0.69326103f));
+  p = ffma2(p, f, make_float2(0.99992806f, 0.99992806f));
+  // p + (n << 23) with n = bits(t) - bits(kRound), in unsigned arithmetic.
+  const uint32_t bias = 0u - (__float_as_uint(kRound) << 23);
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23) + bias),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23) + bias));
 }
 
-// Of every 8 consecutive scores of a row, this many take ex2_poly and the rest
-// the hardware ex2.
+// Of every 8 consecutive scores of a row, this many (an even number) take the
+// FMA-pipe exponential and the rest the hardware ex2.
 #ifndef ATT_EMU_PER8
 #define ATT_EMU_PER8 2
 #endif
@@ -105,52 +130,53 @@ __device__ __forceinline__ void att_load_tile(const CUtensorMap* map, uint64_t* 
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+  constexpr int KS = ATT_K_STAGES;
+  constexpr int VS = ATT_V_STAGES;
   constexpr uint32_t IDESC_S = idesc_f16_f32(ATT_BM, ATT_BN, false, false);
   constexpr uint32_t IDESC_O = idesc_f16_f32(ATT_BM, ATT_D, false, true);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + ATT_TILE_BYTES;       // [2]
-  uint8_t* sV = smem + 3 * ATT_TILE_BYTES;   // [2]
-  uint8_t* sP = smem + 5 * ATT_TILE_BYTES;   // [2]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * ATT_TILE_BYTES);
-  uint64_t* q_full = bars;          // 1
-  uint64_t* k_full = bars + 1;      // 2
-  uint64_t* k_empty = bars + 3;     // 2
-  uint64_t* v_full = bars + 5;      // 2
-  uint64_t* v_empty = bars + 7;     // 2
-  uint64_t* s_full = bars + 9;      // 2
-  uint64_t* s_free = bars + 11;     // 2
-  uint64_t* p_full = bars + 13;     // 1: P_j written (and O rescaled)
-  uint64_t* pv_done = bars + 14;    // 2: P_j V_j finished, per P buffer j%2
-  uint64_t* drain = bars + 16;      // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint8_t* sQ = smem;                                          // [2]
+  uint8_t* sK = smem + ATT_QTILES * ATT_TILE_BYTES;            // [KS]
+  uint8_t* sV = sK + KS * ATT_TILE_BYTES;                      // [VS]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * ATT_TILE_BYTES);
+  uint64_t* q_full = bars;                  // 2
+  uint64_t* s_full = bars + 2;              // 2: S_i(j) in TMEM (and O_i += P_i(j-1) V done)
+  uint64_t* p_full = bars + 4;              // 2: P_i(j) in TMEM (and O_i rescaled)
+  uint64_t* o_full = bars + 6;              // 2: last O_i += P V done
+  uint64_t* drain = bars + 8;               // 1
+  uint64_t* k_full = bars + 9;              // KS
+  uint64_t* k_empty = k_full + KS;          // KS
+  uint64_t* v_full = k_empty + KS;          // VS
+  uint64_t* v_empty = v_full + VS;          // VS
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_empty + VS);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const Watchdog wd{args.status, args.timeout_ns};
-  const int qt = blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int hk = h / (args.heads_q / args.heads_kv);
   const int nkv = (args.C + ATT_BN - 1) / ATT_BN;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], ATT_BM);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(&pv_done[0], 1);
-    mbar_init(&pv_done[1], 1);
-    mbar_init(drain, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -161,190 +187,231 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_O = tmem_base + 256;
 
+  if (warp < 4) {
+    regs_dec<ATT_REGS_LOW>();
   if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (elect_one()) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, ATT_TILE_BYTES);
-      att_load_tile(&tmQ, q_full, sQ, args.layout, qt * ATT_BM, h, b);
-      int j = 0;
-      for (; j < nkv; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(&k_empty[s], ph, wd, SITE_ATT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&k_full[s], ATT_TILE_BYTES);
-        att_load_tile(&tmK, &k_full[s], sK + s * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
-        if (!mbar_wait(&v_empty[s], ph, wd, SITE_ATT_PRODUCER)) {
-          ++j;  // K_j is in flight: drain it below
-          break;
+      const int row0 = blockIdx.x * ATT_CTA_ROWS;
+      mbar_arrive_expect_tx(&q_full[0], ATT_TILE_BYTES);
+      att_load_tile(&tmQ, &q_full[0], sQ, args.layout, row0, h, b);
+      int kj = 0, vj = 0;  // tiles issued
+      bool ok = true;
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int ks = j % KS;
+        if (!mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, wd, SITE_ATT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&k_full[ks], ATT_TILE_BYTES);
+        att_load_tile(&tmK, &k_full[ks], sK + ks * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
+        kj = j + 1;
+        if (j == 0) {
+          mbar_arrive_expect_tx(&q_full[1], ATT_TILE_BYTES);
+          att_load_tile(&tmQ, &q_full[1], sQ + ATT_TILE_BYTES, args.layout, row0 + ATT_BM, h, b);
         }
-        mbar_arrive_expect_tx(&v_full[s], ATT_TILE_BYTES);
-        att_load_tile(&tmV, &v_full[s], sV + s * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
+        const int vs = j % VS;
+        if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, wd, SITE_ATT_PRODUCER)) break;
+        mbar_arrive_expect_tx(&v_full[vs], ATT_TILE_BYTES);
+        att_load_tile(&tmV, &v_full[vs], sV + vs * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
+        vj = j + 1;
       }
-      // Wait for the last copies of every buffer before leaving.
-      mbar_wait(q_full, 0, wd, SITE_ATT_PRODUCER_DRAIN);
-      for (int i = (j > 2 ? j - 2 : 0); i < j; ++i) {
-        mbar_wait(&k_full[i & 1], (i >> 1) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
-        mbar_wait(&v_full[i & 1], (i >> 1) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
-      }
+      // Wait for the last copy into every buffer before leaving.
+      mbar_wait(&q_full[0], 0, wd, SITE_ATT_PRODUCER_DRAIN);
+      if (kj > 0) mbar_wait(&q_full[1], 0, wd, SITE_ATT_PRODUCER_DRAIN);
+      for (int i = (kj > KS ? kj - KS : 0); i < kj; ++i)
+        mbar_wait(&k_full[i % KS], (i / KS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
+      for (int i = (vj > VS ? vj - VS : 0); i < vj; ++i)
+        mbar_wait(&v_full[i % VS], (i / VS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (elect_one()) {
-      bool ok = mbar_wait(q_full, 0, wd, SITE_ATT_MMA_Q);
-      tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
-      for (int j = 0; j <= nkv && ok; ++j) {
-        if (j < nkv) {
-          const int s = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&k_full[s], ph, wd, SITE_ATT_MMA_K)) break;
-          if (!mbar_wait(&s_free[s], ph ^ 1, wd, SITE_ATT_MMA_SFREE)) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + s * ATT_TILE_BYTES);
+      const uint32_t k_addr0 = smem_u32(sK);
+      const uint32_t v_addr0 = smem_u32(sV);
+      // S_i = Q_i K_j^T into TMEM columns [128 i, 128 i + 128).
+      auto issue_s = [&](int i, int ks) {
+        const uint32_t qa = q_addr + i * ATT_TILE_BYTES;
+        const uint32_t ka = k_addr0 + ks * ATT_TILE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < ATT_D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem_base + s * 128, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
-                        IDESC_S, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&k_empty[s]);
-          umma_commit(&s_full[s]);
+        for (int kk = 0; kk < ATT_D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16_ss(tmem_base + i * 128, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024), IDESC_S,
+                      kk > 0 ? 1u : 0u);
         }
-        if (j >= 1) {
-          const int jp = j - 1;
-          const int s = jp & 1;
-          if (!mbar_wait(p_full, jp & 1, wd, SITE_ATT_MMA_P)) break;
-          if (!mbar_wait(&v_full[s], (jp >> 1) & 1, wd, SITE_ATT_MMA_V)) break;
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + s * ATT_TILE_BYTES);
-          const uint32_t pb_addr = p_addr + (jp & 1) * ATT_TILE_BYTES;
+      };
+      // O_i += P_i V: P_i is fp16 pairs in TMEM columns [128 i, 128 i + 64).
+      auto issue_pv = [&](int i, int vs, bool acc) {
+        const uint32_t va = v_addr0 + vs * ATT_TILE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-            const uint64_t adesc = sw128_desc(pb_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-            const uint64_t bdesc = sw128_desc(v_addr + kk * 2048, 16384, 1024);
-            umma_f16_ss(tmem_O, adesc, bdesc, IDESC_O, (jp > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < ATT_BN / 16; ++kk)
+          umma_f16_ts(tmem_base + 256 + i * 128, tmem_base + i * 128 + kk * 8, sw128_desc(va + kk * 2048, 16384, 1024),
+                      IDESC_O, (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&q_full[0], 0, wd, SITE_ATT_MMA_Q) && mbar_wait(&k_full[0], 0, wd, SITE_ATT_MMA_K);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        umma_commit(&s_full[0]);
+        ok = mbar_wait(&q_full[1], 0, wd, SITE_ATT_MMA_Q);
+      }
+      if (ok) {
+        tc_fence_after();
+        issue_s(1, 0);
+        umma_commit(&s_full[1]);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int vs = j % VS;
+        const bool more = j + 1 < nkv;
+        const int ks = (j + 1) % KS;
+        // Q tile 0: O0 += P0 V_j, then S0 of the next key tile.
+        if (!mbar_wait(&p_full[0], j & 1, wd, SITE_ATT_MMA_P) ||
+            !mbar_wait(&v_full[vs], (j / VS) & 1, wd, SITE_ATT_MMA_V)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(0, vs, j > 0);
+        if (more) {
+          if (!mbar_wait(&k_full[ks], ((j + 1) / KS) & 1, wd, SITE_ATT_MMA_K)) {
+            ok = false;
+            break;
           }
-          umma_commit(&v_empty[s]);
-          umma_commit(&pv_done[jp & 1]);
+          tc_fence_after();
+          issue_s(0, ks);
+          umma_commit(&s_full[0]);
+        } else {
+          umma_commit(&o_full[0]);
+        }
+        // Q tile 1.
+        if (!mbar_wait(&p_full[1], j & 1, wd, SITE_ATT_MMA_P)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(1, vs, j > 0);
+        umma_commit(&v_empty[vs]);
+        if (more) {
+          issue_s(1, ks);
+          umma_commit(&s_full[1]);
+          umma_commit(&k_empty[ks]);
+        } else {
+          umma_commit(&o_full[1]);
         }
       }
       umma_commit(drain);
       mbar_wait(drain, 0, wd, SITE_ATT_MMA_DRAIN);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
     // ---------------------------------------------------------- softmax
-    const int q = warp & 3;
+    regs_inc<ATT_REGS_HIGH>();
+    const int ti = (warp - 4) >> 2;  // Q tile of this warpgroup
+    const int q = warp & 3;          // TMEM lane quadrant
     const int r = q * 32 + lane;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t p_row0 = smem_u32(sP) + r * 128;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t tS = tmem_base + ti * 128 + lane_off;
+    const uint32_t tO = tmem_base + 256 + ti * 128 + lane_off;
+    const float sl2 = args.scale_log2;
     float m = -INFINITY;  // running max, log2 domain (possibly stale by < 8)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      const int s = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s], (j >> 1) & 1, wd, SITE_ATT_SOFTMAX_S));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[ti], j & 1, wd, SITE_ATT_SOFTMAX_S));
       if (!ok) break;
       tc_fence_after();
       float x[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + s * 128 + c * 32, v);
+      {
+        uint32_t v0[32], v1[32], v2[32], v3[32];
+        tmem_ld_32x32b_x32(tS + 0, v0);
+        tmem_ld_32x32b_x32(tS + 32, v1);
+        tmem_ld_32x32b_x32(tS + 64, v2);
+        tmem_ld_32x32b_x32(tS + 96, v3);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+        for (int i = 0; i < 32; ++i) {
+          x[i] = __uint_as_float(v0[i]);
+          x[32 + i] = __uint_as_float(v1[i]);
+          x[64 + i] = __uint_as_float(v2[i]);
+          x[96 + i] = __uint_as_float(v3[i]);
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[s]);
       const int valid = args.C - j * ATT_BN;
       if (valid < ATT_BN) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (i >= valid) x[i] = -INFINITY;
       }
-      // Row max of the raw scores (scale > 0 commutes with max), eight
-      // independent partial maxima so the comparisons pipeline.
-      float pm[8];
+      // Row max of the raw scores (scale > 0 commutes with max): four
+      // independent chains of three-input maxima.
+      // Chains start at x[0..3], take 4..123 eight at a time; 124..127 join last.
+      float pm[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) pm[e] = x[e];
+      for (int i = 4; i < 124; i += 8)
 #pragma unroll
-      for (int i = 8; i < 128; i += 8)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) pm[e] = fmaxf(pm[e], x[i + e]);
-      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) *
-                       args.scale_log2;
-
+        for (int e = 0; e < 4; ++e) pm[e] = fmax3(pm[e], x[i + e], x[i + 4 + e]);
+      const float mx = fmax3(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]),
+                             fmaxf(fmaxf(x[124], x[125]), fmaxf(x[126], x[127]))) *
+                       sl2;
       const bool grow = (mx > m + 8.0f);
       const float m_new = grow ? mx : m;
       const float factor = grow ? ex2_approx(m - m_new) : 1.0f;
-      const bool warp_rescale = j > 0 && __any_sync(0xffffffffu, grow);
-      // O may be rescaled only once P_{j-1} V_{j-1} has finished.
-      if (warp_rescale) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, wd, SITE_ATT_SOFTMAX_PV));
-        if (!ok) break;
-        tc_fence_after();
-      }
-      // P buffer j%2 was last read by P_{j-2} V_{j-2}.
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, wd, SITE_ATT_SOFTMAX_PV));
-        if (!ok) break;
-      }
-      if (warp_rescale) {
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // Rescale this warp's O rows in TMEM (lanes without growth use 1.0).
+        // O_i += P_i(j-1) V has completed: the commit of S_i(j) covers it.
 #pragma unroll 1
-        for (int c = 0; c < ATT_D / 16; ++c) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(tmem_O + (static_cast<uint32_t>(q * 32) << 16) + c * 16, v);
+        for (int c = 0; c < ATT_D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tO + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * factor);
-          tmem_st_32x32b_x16(tmem_O + (static_cast<uint32_t>(q * 32) << 16) + c * 16, v);
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * factor);
+          tmem_st_32x32b_x32(tO + c * 32, v);
         }
-        tmem_st_wait();
       }
       l *= factor;
       m = m_new;
-      // P = 2^(x * scale_log2 - m) as fp16 into the swizzled K-major P tile
-      // (two 64-key halves) of buffer j%2: one FFMA + exp per element, eight
-      // partial sums so the additions stay independent.
-      const uint32_t p_row = p_row0 + (j & 1) * ATT_TILE_BYTES;
-      const float neg_m = -m;
-      float ls[8];
+      // P = 2^(x * scale_log2 - m): one packed FFMA per pair, an exponential
+      // per element, packed partial sums; fp16 pairs over the S row.
+      const float2 sc = make_float2(sl2, sl2);
+      const float2 nm = make_float2(-m, -m);
+      float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ls[e] = 0.f;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float p[8];
+        for (int c = 0; c < 8; ++c) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float arg = fmaf(x[c * 8 + e], args.scale_log2, neg_m);
-          p[e] = (e >= 8 - ATT_EMU_PER8) ? ex2_poly(arg) : ex2_approx(arg);
-          ls[e] += p[e];
+          for (int e = 0; e < 4; ++e) {
+            const int idx = half * 64 + c * 8 + 2 * e;
+            const float2 a = ffma2(make_float2(x[idx], x[idx + 1]), sc, nm);
+            float2 p;
+            if (2 * e >= 8 - ATT_EMU_PER8) {
+              p = ex2_poly2(a);
+            } else {
+              p.x = ex2_approx(a.x);
+              p.y = ex2_approx(a.y);
+            }
+            acc[e] = fadd2(acc[e], p);
+            pk[c * 4 + e] = pack_half2(p.x, p.y);
+          }
         }
-        const uint32_t dst = p_row + (c >> 3) * 16384 + (((c & 7) ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(pack_half2(p[0], p[1])),
-                     "r"(pack_half2(p[2], p[3])), "r"(pack_half2(p[4], p[5])), "r"(pack_half2(p[6], p[7]))
-                     : "memory");
+        tmem_st_32x32b_x32(tS + half * 32, pk);
       }
-      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-      fence_proxy_async_smem();
+      const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
+      l += s01.x + s01.y;
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[ti]);
     }
-    if (ok && nkv > 0) {
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, wd, SITE_ATT_SOFTMAX_PV));
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_full[ti], 0, wd, SITE_ATT_SOFTMAX_O));
       if (ok) {
         tc_fence_after();
-        const int row = qt * ATT_BM + r;
+        const int row = blockIdx.x * ATT_CTA_ROWS + ti * ATT_BM + r;
         const float inv_l = 1.0f / l;
         __half* dst = nullptr;
         if (row < args.R) {
@@ -356,7 +423,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < ATT_D / 32; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem_O + (static_cast<uint32_t>(q * 32) << 16) + c * 32, v);
+          tmem_ld_32x32b_x32(tO + c * 32, v);
           tmem_ld_wait();
           if (dst) {
 #pragma unroll

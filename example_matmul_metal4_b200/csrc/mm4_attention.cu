@@ -102,7 +102,21 @@ mm4_status mm4_attention_fwd(const mm4_attention_plan* p, const void* Q, const v
 
   rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_fwd_sm100_kernel), ATT_SMEM_BYTES);
   if (rc != MM4_OK) return rc;
-  dim3 grid((d.rows + ATT_BM - 1) / ATT_BM, d.heads_q, d.batch);
+  {
+    // The kernel moves registers between warpgroups (setmaxnreg); that only
+    // completes if the launch allocates at least ATT_REGS_NEEDED per thread.
+    static int launch_regs = -1;
+    if (launch_regs < 0) {
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(attention_fwd_sm100_kernel));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(attention_fwd_sm100_kernel)");
+      launch_regs = fa.numRegs;
+    }
+    if (launch_regs < ATT_REGS_NEEDED)
+      return fail(MM4_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs %d", launch_regs,
+                  ATT_REGS_NEEDED);
+  }
+  dim3 grid((d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS, d.heads_q, d.batch);
   if (grid.y > 65535 || grid.z > 65535) return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int i = 0; i < duplicated_count; ++i) {

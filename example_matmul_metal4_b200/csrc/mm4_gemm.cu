@@ -6,6 +6,7 @@
 // time; mm4 instead selects one of a fixed set of template instances
 // (BN x operand majors x epilogue mode) when the plan is created.
 #include <algorithm>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -55,6 +56,17 @@ mm4_status run_simt(const mm4_gemm_plan* p, const void* A, const void* B, const 
   return MM4_OK;
 }
 
+// MM4_SPLITK_COOPERATIVE=0 selects the last-arriver finalize even where every
+// work unit fits on the device at once (profilers that replay kernels may not
+// support cooperative launches of clusters).
+bool cooperative_finalize_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MM4_SPLITK_COOPERATIVE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const void* bias, void* C, float* C32,
                   void* ws, size_t ws_bytes, cudaStream_t st) {
   DeviceInfo info;
@@ -85,7 +97,7 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
     args.ws = static_cast<float*>(ws);
     args.counters = reinterpret_cast<int*>(static_cast<char*>(ws) + p->ws_counter_offset);
     const int ctas = p->pair ? 2 * args.num_units : args.num_units;
-    args.coop_finalize = (ctas <= info.sm_count) ? 1 : 0;
+    args.coop_finalize = (ctas <= info.sm_count && cooperative_finalize_enabled()) ? 1 : 0;
     mode = out_f32 ? MODE_SPLITK_F32 : MODE_SPLITK_F16;
   } else {
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
