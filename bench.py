@@ -23,9 +23,12 @@ distributions):
   is fixed as N grows (weak scaling) and `value` is the whole-job rate.
 
 Timing: W untimed warm-up steps, then K timed steps, each bracketed by CUDA
-events on the launching stream, with a 512 MiB write between steps to flush
-L2 (126 MB) outside the events. Barrier + synchronize on both sides; the
-reported time is the max over ranks.
+events on the launching stream, with every step's inputs out of L2: HBM-bound
+workloads read the next of several device copies of their inputs each step
+(together well over the 126 MB L2), tensor-bound ones get a 512 MiB write
+between steps that flushes L2 outside the events (--l2 rotate|flush forces
+either). Barrier + synchronize on both
+sides; the reported time is the max over ranks.
 
 `--impl reference` times the reference's CPU implementation of the path (the
 C restatement of its Swift validation loops under oracle/, all host threads)
@@ -195,7 +198,7 @@ class Dist:
         import datetime
         import torch.distributed as dist
         if self.world > 1:
-            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=60))
             self.pg = dist
 
     def barrier(self):
@@ -279,17 +282,20 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 def time_steps(step, steps, warmup, flush, stream, dist):
-    """Per-step CUDA events on `stream`; L2 flush between steps outside events."""
+    """Per-step CUDA events on `stream`; with `flush`, an L2 flush between steps outside the events
+    (without it the step rotates its inputs, see input_sets)."""
     import torch
     for _ in range(warmup):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         step()
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     events = []
     for _ in range(steps):
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record(stream)
@@ -302,15 +308,21 @@ def time_steps(step, steps, warmup, flush, stream, dist):
     return [s.elapsed_time(e) for s, e in events]
 
 
-def burn(step, flush, seconds):
-    """Repeats the step (with L2 flushes) for about `seconds`, untimed."""
+def burn(step, flush, seconds, dist):
+    """Repeats the step (with L2 flushes) for about `seconds`, untimed. Ranks run the same number of
+    steps (the step may hold a collective): after every block of 4 they agree, by a MAX all-reduce,
+    whether any rank still wants to continue."""
     import torch
     t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end:
+    while True:
         for _ in range(4):
-            flush.zero_()
+            if flush is not None:
+                flush.zero_()
             step()
         torch.cuda.synchronize()
+        more = 1.0 if time.perf_counter() < t_end else 0.0
+        if dist.max(more) == 0.0:
+            return
 
 
 # ---------------------------------------------------------------------------
@@ -318,7 +330,35 @@ def burn(step, flush, seconds):
 # Each returns (step, e2e_step, (h2d, d2h) bytes, kernel name, launches/step, scaling).
 # ---------------------------------------------------------------------------
 
-def build_gemm(w, dist, dev, gen):
+L2_BYTES = 126 * 1000 * 1000  # B200 L2
+
+
+def input_sets(first, l2):
+    """Device copies of a step's inputs for cold-L2 timing without a flush.
+
+    l2 == "rotate": 1 + ceil(2 * L2 / bytes) copies (at least 2); a step uses the next copy, so
+    between two uses of one copy at least twice the L2 size of other inputs has been read and the
+    copy is evicted. l2 == "flush": just `first` (the caller flushes L2 between steps)."""
+    import torch
+    if l2 != "rotate":
+        return [first]
+    nbytes = sum(t.numel() * t.element_size() for t in first.values())
+    n = max(2, 1 + math.ceil(2 * L2_BYTES / nbytes))
+    return [first] + [{k: v.clone() for k, v in first.items()} for _ in range(n - 1)]
+
+
+def cycling(sets):
+    """Returns a function giving the next input set on each call."""
+    state = [0]
+
+    def nxt():
+        cur = sets[state[0]]
+        state[0] = (state[0] + 1) % len(sets)
+        return cur
+    return nxt
+
+
+def build_gemm(w, dist, dev, gen, l2):
     import torch
     from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan
     from example_matmul_metal4_b200.gemm import splitk_finalize
@@ -333,6 +373,8 @@ def build_gemm(w, dist, dev, gen):
         B = full["B"][k0:k1].contiguous()
         bias = full["bias"]
         del full
+        sets = input_sets({"A": A, "B": B}, l2)
+        nxt = cycling(sets)
         plan = GemmPlan(GEMMDimensions(M, N, k1 - k0), transpose=(False, False), bias=False,
                         buildOptions=BuildOptions(splitK=splitk_per_rank(w.split, P)))
         C32 = torch.empty((M, N), dtype=torch.float32, device=dev)
@@ -340,20 +382,25 @@ def build_gemm(w, dist, dev, gen):
         ws = plan.workspace(dev)
 
         def step():
-            plan.partial(A, B, C32=C32, workspace=ws)
+            t = nxt()
+            plan.partial(t["A"], t["B"], C32=C32, workspace=ws)
             reduce_partials(C32, dst=0)
             if r == 0:
                 splitk_finalize(C32, bias, C=C)
-        return step, None, None, plan.kernel_name + " + nccl reduce + finalize", (2 if r == 0 else 1), "strong"
+        return (step, None, None, plan.kernel_name + " + nccl reduce + finalize", (2 if r == 0 else 1), "strong",
+                len(sets))
     t = w.inputs(dev, gen)
     A, B, bias = t["A"], t["B"], t["bias"]
+    sets = input_sets({"A": A, "B": B}, l2)
+    nxt = cycling(sets)
     plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
                     buildOptions=BuildOptions(splitK=w.split))
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
     ws = plan.workspace(dev)
 
     def step():
-        plan.run(A, B, bias, C=C, workspace=ws)
+        t = nxt()
+        plan.run(t["A"], t["B"], bias, C=C, workspace=ws)
 
     hA, hB, hb = A.cpu().pin_memory(), B.cpu().pin_memory(), bias.cpu().pin_memory()
     hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
@@ -365,19 +412,22 @@ def build_gemm(w, dist, dev, gen):
         plan.run(A, B, bias, C=C, workspace=ws)
         hC.copy_(C, non_blocking=True)
     e2e_bytes = (A.numel() * 2 + B.numel() * 2 + bias.numel() * 2, C.numel() * 2)
-    return step, e2e_step, e2e_bytes, plan.kernel_name, 1, "weak"
+    return step, e2e_step, e2e_bytes, plan.kernel_name, 1, "weak", len(sets)
 
 
-def build_attention(w, dist, dev, gen):
+def build_attention(w, dist, dev, gen, l2):
     import torch
     from example_matmul_metal4_b200.attention import AttentionDimensions, AttentionPlan
     plan = AttentionPlan(AttentionDimensions(w.S, w.S, w.D, w.H, w.H), batch=w.B)
     t = w.inputs(dev, gen)
     Q, K, V = t["Q"], t["K"], t["V"]
     O = torch.empty_like(Q)
+    sets = input_sets({"Q": Q, "K": K, "V": V}, l2)
+    nxt = cycling(sets)
 
     def step():
-        plan.run(Q, K, V, O=O)
+        t = nxt()
+        plan.run(t["Q"], t["K"], t["V"], O=O)
 
     hQ, hK, hV = Q.cpu().pin_memory(), K.cpu().pin_memory(), V.cpu().pin_memory()
     hO = torch.empty(O.shape, dtype=O.dtype).pin_memory()
@@ -388,10 +438,10 @@ def build_attention(w, dist, dev, gen):
         V.copy_(hV, non_blocking=True)
         plan.run(Q, K, V, O=O)
         hO.copy_(O, non_blocking=True)
-    return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "weak"
+    return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "weak", len(sets)
 
 
-def build_conv(w, dist, dev, gen):
+def build_conv(w, dist, dev, gen, l2):
     import torch
     from example_matmul_metal4_b200.conv import (WEIGHTS_ODHWI, WEIGHTS_OHWI, Conv2DDimensions, Conv3DDimensions,
                                                  ConvPlan)
@@ -404,9 +454,12 @@ def build_conv(w, dist, dev, gen):
     t = w.inputs(dev, gen)
     x, wt, bias = t["x"], t["w"], t["bias"]
     y = torch.empty(plan.out_shape, dtype=torch.float16, device=dev)
+    sets = input_sets({"x": x, "w": wt}, l2)
+    nxt = cycling(sets)
 
     def step():
-        plan.run(x, wt, bias, y=y)
+        t = nxt()
+        plan.run(t["x"], t["w"], bias, y=y)
 
     hx, hw, hb = x.cpu().pin_memory(), wt.cpu().pin_memory(), bias.cpu().pin_memory()
     hy = torch.empty(plan.out_shape, dtype=torch.float16).pin_memory()
@@ -417,7 +470,8 @@ def build_conv(w, dist, dev, gen):
         bias.copy_(hb, non_blocking=True)
         plan.run(x, wt, bias, y=y)
         hy.copy_(y, non_blocking=True)
-    return step, e2e_step, ((x.numel() + wt.numel() + bias.numel()) * 2, y.numel() * 2), plan.kernel_name, 1, "weak"
+    return (step, e2e_step, ((x.numel() + wt.numel() + bias.numel()) * 2, y.numel() * 2), plan.kernel_name, 1,
+            "weak", len(sets))
 
 
 def run_mm4(args, w, dist, peaks):
@@ -432,8 +486,8 @@ def run_mm4(args, w, dist, peaks):
     gen.manual_seed(w.seed * 1000003 + (0 if same_inputs else dist.rank))
     builder = (build_gemm if isinstance(w, GemmWorkload) else
                build_attention if isinstance(w, AttentionWorkload) else build_conv)
-    step, e2e_step, e2e_bytes, kernel_name, launches, scaling = builder(w, dist, dev, gen)
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    step, e2e_step, e2e_bytes, kernel_name, launches, scaling, nsets = builder(w, dist, dev, gen, args.l2)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if args.l2 == "flush" else None
 
     step()
     torch.cuda.synchronize()
@@ -441,9 +495,9 @@ def run_mm4(args, w, dist, peaks):
 
     clocks = ClockSampler(dist.local_rank)
     clocks.start()
-    burn(step, flush, 0.6)
+    burn(step, flush, 0.6, dist)
     per_step = time_steps(step, args.steps, args.warmup, flush, stream, dist)
-    burn(step, flush, 0.3)
+    burn(step, flush, 0.3, dist)
     clk = clocks.stop()
     sync_check()
     ms = dist.max(sum(per_step) / len(per_step))
@@ -470,7 +524,7 @@ def run_mm4(args, w, dist, peaks):
                 "algorithmic_bytes": w.bytes(), "algorithmic_flops": w.flops(),
                 "traffic": load_traffic(w.name), "kernel": kernel_name, "kernel_ms": ms}
     return dict(value=value, ms=ms, clocks=clk, e2e=e2e, roofline=roof, launches=launches * args.steps,
-                kernel=kernel_name, scaling=scaling)
+                kernel=kernel_name, scaling=scaling, nsets=nsets)
 
 
 # ---------------------------------------------------------------------------
@@ -552,9 +606,15 @@ def main():
     ap.add_argument("--impl", default="mm4", choices=["mm4", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--l2", default="auto", choices=["auto", "rotate", "flush"],
+                    help="keep inputs out of L2 by rotating device copies of them or by a 512 MiB write between "
+                         "steps; auto: rotate for HBM-bound workloads (a write flush leaves ~126 MB of dirty lines "
+                         "whose write-back would land inside the timed kernel), flush for tensor-bound ones")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]()
+    if args.l2 == "auto":
+        args.l2 = "rotate" if w.bound == "hbm" else "flush"
     dist = Dist(args.gpus)
     peaks = load_peaks()
     base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -562,6 +622,9 @@ def main():
             "data": "synthetic (seeded torch generator; BASELINE shapes and distributions)"}
     cfg = dict(w.config(), l2="flushed between steps (512 MiB write outside the timed events)",
                baseline_config_index=w.config_index)
+    if args.l2 == "rotate":
+        cfg["l2"] = ("inputs larger than L2: each step reads the next of {n} device copies of its inputs, so "
+                     "at least 2 x 126 MB of other inputs pass through L2 between two uses of a copy; no flush")
 
     if args.impl == "reference":
         if dist.rank != 0:
@@ -588,6 +651,7 @@ def main():
         if args.gpus == 1 and not args.no_cpu_baseline:
             cpu = cpu_sample(w, seconds_hint=args.cpu_seconds)
         cfg["kernel"] = res["kernel"]
+        cfg["l2"] = cfg["l2"].replace("{n}", str(res["nsets"]))
         cfg["parallelism"] = ("single GPU" if args.gpus == 1 else
                               ("K-shard + NCCL fp32 reduce" if res["scaling"] == "strong" else
                                f"{args.gpus} independent shards, no collective"))

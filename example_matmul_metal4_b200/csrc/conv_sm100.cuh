@@ -211,7 +211,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       mma_role<BN, false, B_MN, STAGES, Cfg::STAGE_BYTES, Cfg::A_BYTES, !A_TMA>(args, ring, full, empty, tmem_full,
                                                                            tmem_empty, drain, tmem_base, wd);
   } else if (warp < 6) {
-    epilogue_role<BN, MODE_DIRECT_F16>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, wd, warp, lane);
+    epilogue_role<BN, MODE_DIRECT_F16>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, nullptr, wd, warp,
+                                       lane);
   } else if (!A_TMA) {
     // ------------------------------------------------ activation gather
     const int gt = threadIdx.x - CONV_GATHER_T0;  // 0..127

@@ -138,9 +138,14 @@ inline void gemm_plan_args(const mm4_gemm_plan* p, GemmArgs* a) {
 }
 
 // Grid for the plan: one CTA (or CTA pair) per work unit, at most one per SM.
+// Split-K plans get one CTA (pair) per (split, M-tile) when that fits, so each
+// walks the N-tiles of its k-slab (see gemm_decode_unit).
 inline int gemm_grid(const mm4_gemm_plan* p, int num_units, int sm_count) {
-  if (p->pair) return 2 * std::min(num_units, sm_count / 2);
-  return std::min(num_units, sm_count);
+  int slots = p->pair ? sm_count / 2 : sm_count;
+  int want = num_units;
+  if (p->splits > 1) want = std::min(want, p->splits * p->num_m_tiles);
+  const int n = std::min(want, slots);
+  return p->pair ? 2 * n : n;
 }
 
 inline mm4_status gemm_dispatch(const mm4_gemm_plan* p, int mode, const CUtensorMap& ta, const CUtensorMap& tb,

@@ -49,7 +49,7 @@ struct GemmArgs {
   __half* C;              // [M][N] fp16 output (F16 modes)
   float* C32;             // [M][N] fp32 output (F32 modes)
   float* ws;              // [num_m_tiles*128][ws_ld] fp32, split-K only
-  int* counters;          // [num_tiles], split-K only
+  unsigned long long* counters;  // one arrival count per 128-row half tile, split-K only
   int ws_ld;
   int coop_finalize;      // split-K: all units co-resident (cooperative launch), slices finalized in parallel
   // Output row map of the direct epilogue. 0: tile row r is output row
@@ -65,6 +65,12 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 
+// Split-K epilogue staging: per epilogue warp a 32 x 32 fp32 block, rows
+// padded to 36 floats so both the row-wise writes and the transposed reads
+// are free of bank conflicts.
+constexpr int EPI_STAGE_LD = 36;
+constexpr int EPI_STAGE_BYTES = 4 * 32 * EPI_STAGE_LD * 4;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KB
@@ -76,8 +82,8 @@ struct GemmCfg {
   static constexpr int N_INSTR = BN < 256 ? BN : 256;    // UMMA N per instruction
   static constexpr int N_HALVES = BN / N_INSTR;
   static constexpr int B_BOX_N = BN < 256 ? BN : 256;    // K-major B: TMA box rows
-  // ring + barriers/slots + alignment slack
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+  // ring + split-K staging + barriers/slots + alignment slack
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 256 + 1024;
 };
 
 // Wait-site ids recorded with MM4_ERR_TIMEOUT.
@@ -92,31 +98,36 @@ enum : int {
 };
 
 struct GemmUnit {
-  int mt, nt, tile, kb0, kb1;
+  int mt, nt, tile, split, kb0, kb1;
 };
 
 __device__ __forceinline__ GemmUnit gemm_decode_unit(const GemmArgs& a, int u) {
   GemmUnit w;
-  int t, split;
   if (a.splits > 1) {
-    // Units of one k-split are adjacent so co-resident CTAs share A/B k-slabs in L2.
-    split = u / a.num_tiles;
-    t = u - split * a.num_tiles;
+    // Split-K: N-tile-major, then split, then M-tile. With the grid at
+    // splits * num_m_tiles CTAs (pairs) each one keeps its (split, M-tile)
+    // and walks the N-tiles, so its A k-slab is re-read from L2 and the
+    // reduction of one N-tile overlaps the main loop of the next; all units
+    // of one N-tile run together and share their B k-slabs in L2.
+    const int per_n = a.splits * a.num_m_tiles;
+    w.nt = u / per_n;
+    const int r = u - w.nt * per_n;
+    w.split = r / a.num_m_tiles;
+    w.mt = r - w.split * a.num_m_tiles;
   } else {
-    split = 0;
-    t = u;
+    // Grouped raster: walk group_m M-tiles down a column of N-tiles.
+    w.split = 0;
+    const int group_size = a.group_m * a.num_n_tiles;
+    const int group = u / group_size;
+    const int first_m = group * a.group_m;
+    const int gm = min(a.num_m_tiles - first_m, a.group_m);
+    const int r = u - group * group_size;
+    w.mt = first_m + r % gm;
+    w.nt = r / gm;
   }
-  // Grouped raster: walk group_m M-tiles down a column of N-tiles.
-  const int group_size = a.group_m * a.num_n_tiles;
-  const int group = t / group_size;
-  const int first_m = group * a.group_m;
-  const int gm = min(a.num_m_tiles - first_m, a.group_m);
-  const int r = t - group * group_size;
-  w.mt = first_m + r % gm;
-  w.nt = r / gm;
   w.tile = w.mt * a.num_n_tiles + w.nt;
-  w.kb0 = static_cast<int>((static_cast<long long>(split) * a.kb_total) / a.splits);
-  w.kb1 = static_cast<int>((static_cast<long long>(split + 1) * a.kb_total) / a.splits);
+  w.kb0 = static_cast<int>((static_cast<long long>(w.split) * a.kb_total) / a.splits);
+  w.kb1 = static_cast<int>((static_cast<long long>(w.split + 1) * a.kb_total) / a.splits);
   return w;
 }
 
@@ -199,7 +210,8 @@ __device__ __forceinline__ void mma_role(const GemmArgs& args, uint8_t* ring, ui
 template <int BN, int MODE, bool PAIR = false>
 __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tmem_full, uint64_t* tmem_empty,
                                               uint32_t tmem_base, volatile int* s_vote, volatile int* s_last,
-                                              const Watchdog& wd, int warp, int lane, uint32_t rank = 0) {
+                                              float* stage, const Watchdog& wd, int warp, int lane,
+                                              uint32_t rank = 0) {
   constexpr bool SPLITK = (MODE == MODE_SPLITK_F16 || MODE == MODE_SPLITK_F32);
   constexpr bool OUT_F32 = (MODE == MODE_DIRECT_F32 || MODE == MODE_SPLITK_F32);
   constexpr int ACC_BUFS = (BN == 512) ? 1 : 2;
@@ -236,12 +248,16 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
     }
     const int col0 = w.nt * BN;
 
+    // Split-K: each split starts at a different 32-column chunk, so the
+    // splits of a tile do not all reduce into the same lines at once.
+    const int rot = SPLITK ? w.split & (BN / 32 - 1) : 0;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int ci = 0; ci < BN / 32; ++ci) {
+      const int c = (ci + rot) & (BN / 32 - 1);
       uint32_t r[32];
       tmem_ld_32x32b_x32(taddr + c * 32, r);
       tmem_ld_wait();
-      if (c == BN / 32 - 1) {
+      if (ci == BN / 32 - 1) {
         tc_fence_before();
         if (PAIR)
           mbar_arrive_cluster(mapa_shared(smem_u32(&tmem_empty[acc]), 0));
@@ -250,12 +266,23 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       }
       const int cbase = col0 + c * 32;
       if constexpr (SPLITK) {
-        float* dst = args.ws + static_cast<size_t>(row) * args.ws_ld + cbase;
+        // Transpose the warp's 32 rows x 32 columns through shared memory so
+        // that each red instruction covers four whole 128-byte rows (eight
+        // lanes per row) instead of 32 half-used sectors.
+        float* wst = stage + q * (32 * EPI_STAGE_LD);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          red_add_v4_f32(dst + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                         __uint_as_float(r[j + 3]));
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<uint4*>(wst + lane * EPI_STAGE_LD + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        __syncwarp();
+        const int sub_r = lane >> 3;
+        const int sub_c = (lane & 7) * 4;
+        float* dst = args.ws + static_cast<size_t>(row_base + q * 32 + sub_r) * args.ws_ld + cbase + sub_c;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 v = *reinterpret_cast<const float4*>(wst + (k * 4 + sub_r) * EPI_STAGE_LD + sub_c);
+          red_add_v4_f32(dst + static_cast<size_t>(k * 4) * args.ws_ld, v.x, v.y, v.z, v.w);
         }
+        __syncwarp();
       } else if constexpr (OUT_F32) {
         if (row_ok) {
           float* dst = args.C32 + static_cast<size_t>(row) * args.N + cbase;
@@ -307,24 +334,27 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
     }
 
     if constexpr (SPLITK) {
-      // Publish this unit's partial, then count arrivals for the tile.
-      // counters[2*tile] counts arrivals, counters[2*tile+1] departures.
+      // Publish this unit's partial, then count arrivals for the tile. The
+      // 64-bit arrival counters only grow: the launch's arrivals for a tile
+      // are the values [e * splits, (e + 1) * splits) for some e, so no reset
+      // is needed between launches.
       __threadfence();
       named_barrier(1, 128);
       const int ctr_tile = PAIR ? 2 * w.tile + static_cast<int>(rank) : w.tile;  // per 128-row half
-      int* arrive_ctr = &args.counters[2 * ctr_tile];
-      int* depart_ctr = arrive_ctr + 1;
+      unsigned long long* arrive_ctr = &args.counters[ctr_tile];
       if (ethread == 0) {
-        const int prev = atomicAdd(arrive_ctr, 1);
+        const unsigned long long splits = static_cast<unsigned long long>(args.splits);
+        const unsigned long long prev = atomicAdd(arrive_ctr, 1ull);
         if (!args.coop_finalize) {
-          *s_last = (prev == args.splits - 1) ? 1 : 0;
+          *s_last = (prev % splits == splits - 1) ? 1 : 0;
         } else {
           // All units are co-resident (cooperative launch): wait, bounded,
           // until every split of this tile has published its partial.
+          const unsigned long long target = (prev / splits + 1) * splits;
           int ok = 1;
           const uint64_t t0 = globaltimer_ns();
           uint32_t spins = 0;
-          while (*reinterpret_cast<volatile int*>(arrive_ctr) < args.splits) {
+          while (*reinterpret_cast<volatile unsigned long long*>(arrive_ctr) < target) {
             if ((++spins & 63u) == 0 &&
                 (aborted(wd.status) || globaltimer_ns() - t0 > wd.limit_ns)) {
               record_error(wd.status, MM4_ERR_TIMEOUT, SITE_GEMM_EPI_TILE_RENDEZVOUS);
@@ -339,9 +369,8 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       int r_begin = 0, r_end = 0;  // tile rows this CTA finalizes
       if (*s_last) {
         if (args.coop_finalize) {
-          const int split = u / args.num_tiles;
-          r_begin = (split * GEMM_BM) / args.splits;
-          r_end = ((split + 1) * GEMM_BM) / args.splits;
+          r_begin = (w.split * GEMM_BM) / args.splits;
+          r_end = ((w.split + 1) * GEMM_BM) / args.splits;
         } else {
           r_end = GEMM_BM;
         }
@@ -361,13 +390,25 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
           if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
           if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
         }
-#pragma unroll 4
-        for (int rr = r_begin + tr; rr < r_end; rr += RPI) {
+        // Up to four rows per thread in flight: all loads first, then the
+        // stores, so the L2 round trips overlap.
+        for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
+          float4 s4v[4];
+#pragma unroll
+          for (int bb = 0; bb < 4; ++bb) {
+            const int rr = rr0 + bb * RPI;
+            if (rr < r_end)
+              s4v[bb] = __ldcg(reinterpret_cast<const float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+          }
+#pragma unroll
+          for (int bb = 0; bb < 4; ++bb) {
+          const int rr = rr0 + bb * RPI;
+          if (rr >= r_end) break;
           const int grow = row_base + rr;
-          float4* src = reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc);
-          const float4 s4 = __ldcg(src);
-          __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+          __stcg(reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc),
+                 make_float4(0.f, 0.f, 0.f, 0.f));
           if (grow >= args.M) continue;
+          const float4 s4 = s4v[bb];
           const float o0 = s4.x + b0, o1 = s4.y + b1, o2 = s4.z + b2, o3 = s4.w + b3;
           if constexpr (OUT_F32) {
             float* dst = args.C32 + static_cast<size_t>(grow) * args.N + gc;
@@ -393,18 +434,6 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
               if (gc + 3 < args.N) dst[3] = __float2half_rn(o3);
             }
           }
-        }
-      }
-      // Leave the counters at zero for the next launch.
-      if (!args.coop_finalize) {
-        if (*s_last && ethread == 0) *arrive_ctr = 0;
-      } else if (*s_last) {
-        named_barrier(1, 128);
-        if (ethread == 0) {
-          __threadfence();
-          if (atomicAdd(depart_ctr, 1) == args.splits - 1) {
-            *arrive_ctr = 0;
-            *depart_ctr = 0;
           }
         }
       }
@@ -424,7 +453,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + EPI_STAGE_BYTES);
   uint64_t* full = bars;                  // [STAGES]
   uint64_t* empty = bars + STAGES;        // [STAGES]
   uint64_t* tmem_full = bars + 2 * STAGES;   // [2]
@@ -507,7 +537,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mma_role<BN, A_MN, B_MN, STAGES, Cfg::STAGE_BYTES, Cfg::A_BYTES, false>(args, ring, full, empty, tmem_full,
                                                                            tmem_empty, drain, tmem_base, wd);
   } else {
-    epilogue_role<BN, MODE>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, wd, warp, lane);
+    epilogue_role<BN, MODE>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, epi_stage, wd, warp, lane);
   }
 
   tc_fence_before();

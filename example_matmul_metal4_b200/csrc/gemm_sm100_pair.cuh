@@ -37,7 +37,7 @@ struct PairCfg {
   static constexpr int ACC_BUFS = (BN == 512) ? 1 : 2;
   static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr int N_HALVES = BN / 256;                  // MMA instructions (N = 256) per k-step
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 256 + 1024;
 };
 
 enum : int {
@@ -61,7 +61,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  float* epi_stage = reinterpret_cast<float*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES + EPI_STAGE_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tmem_full = bars + 2 * STAGES;
@@ -196,7 +197,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_wait(drain, 0, wd, SITE_PAIR_MMA_DRAIN);
     }
   } else {
-    epilogue_role<BN, MODE, true>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, wd, warp, lane, rank);
+    epilogue_role<BN, MODE, true>(args, tmem_full, tmem_empty, tmem_base, s_vote, s_last, epi_stage, wd, warp, lane,
+                                  rank);
   }
 
   tc_fence_before();

@@ -95,9 +95,14 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
       return fail(MM4_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", ws_bytes, p->ws_bytes);
     if (!aligned16(ws)) return fail(MM4_ERR_WORKSPACE, "workspace must be 16-byte aligned");
     args.ws = static_cast<float*>(ws);
-    args.counters = reinterpret_cast<int*>(static_cast<char*>(ws) + p->ws_counter_offset);
-    const int ctas = p->pair ? 2 * args.num_units : args.num_units;
-    args.coop_finalize = (ctas <= info.sm_count && cooperative_finalize_enabled()) ? 1 : 0;
+    args.counters = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + p->ws_counter_offset);
+    // The cooperative finalize has every split of a tile meet in the
+    // epilogue, so it needs all CTAs co-resident and no two splits of one
+    // tile on the same CTA (pair): one CTA (pair) per (split, M-tile).
+    const int grid = gemm_grid(p, args.num_units, info.sm_count);
+    const int slots = p->pair ? grid / 2 : grid;
+    args.coop_finalize =
+        (grid <= info.sm_count && slots == p->splits * p->num_m_tiles && cooperative_finalize_enabled()) ? 1 : 0;
     mode = out_f32 ? MODE_SPLITK_F32 : MODE_SPLITK_F16;
   } else {
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
@@ -120,6 +125,10 @@ mm4_status validate(const mm4_gemm_desc* d) {
 }  // namespace
 
 extern "C" {
+
+// SM count the tile choice assumes (B200); plans are made without touching a
+// device, launches size their grids from the device's own count.
+constexpr int kPlanSmCount = 148;
 
 mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) {
   if (!out) return fail(MM4_ERR_INVALID, "null plan pointer");
@@ -148,7 +157,19 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   // narrow N; 128 x 512 for wide split-K).
   p->pair = p->tensor_core && d.M >= 256 && d.N >= 256;
   p->bn = (d.N <= 128) ? 128 : 256;
-  if (p->splits > 1 && d.N > 256) p->bn = 512;
+  // Split-K with N > 256: 512-column tiles (all of TMEM, one accumulator)
+  // read the fewest bytes per output, so they win when every (split, tile)
+  // unit gets its own CTA (pair). When units outnumber the CTAs, CTA pairs use
+  // 256 x 256 tiles with two accumulators so one tile's reduction overlaps the
+  // next tile's main loop.
+  if (p->splits > 1 && d.N > 256) {
+    p->bn = 512;
+    if (p->pair) {
+      const int m_tiles = (d.M + 2 * GEMM_BM - 1) / (2 * GEMM_BM);
+      const long long units512 = static_cast<long long>(m_tiles) * ((d.N + 511) / 512) * p->splits;
+      if (units512 > kPlanSmCount / 2) p->bn = 256;
+    }
+  }
   p->num_m_tiles = (d.M + (p->pair ? 2 * GEMM_BM : GEMM_BM) - 1) / (p->pair ? 2 * GEMM_BM : GEMM_BM);
   p->num_n_tiles = (d.N + p->bn - 1) / p->bn;
   p->num_tiles = p->num_m_tiles * p->num_n_tiles;
@@ -158,8 +179,8 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
     const int tile_m = p->pair ? 2 * GEMM_BM : GEMM_BM;
     const size_t acc = static_cast<size_t>(p->num_m_tiles) * tile_m * p->num_n_tiles * p->bn * sizeof(float);
     p->ws_counter_offset = acc;
-    // two counters (arrivals, departures) per 128-row half tile
-    const size_t counters = static_cast<size_t>(p->num_tiles) * (p->pair ? 2 : 1) * 2 * sizeof(int);
+    // one 64-bit arrival counter per 128-row half tile
+    const size_t counters = static_cast<size_t>(p->num_tiles) * (p->pair ? 2 : 1) * sizeof(unsigned long long);
     p->ws_bytes = (acc + counters + 255) & ~static_cast<size_t>(255);
   }
   if (p->tensor_core)

@@ -64,9 +64,10 @@ def test_gemm_plan_validation_and_dispatch():
     rc, h = _gemm(M=512, N=512, K=65536, split_k=32)
     assert rc == 0
     assert b"splitk" in lib.mm4_gemm_plan_kernel_name(h)
-    # 128x512 split-K tiles: fp32 [4*128][512] workspace + 2 counters per tile, rounded to 256 bytes
-    assert b"BN=512" in lib.mm4_gemm_plan_kernel_name(h)
-    assert lib.mm4_gemm_workspace_size(h) == ((512 * 512 * 4 + 4 * 2 * 4 + 255) // 256) * 256
+    # 256x512 CTA-pair split-K tiles (2 of them): fp32 [512][512] workspace + one 64-bit counter
+    # per 128-row half tile, rounded to 256 bytes
+    assert b"BN=512" in lib.mm4_gemm_plan_kernel_name(h) and b"pair" in lib.mm4_gemm_plan_kernel_name(h)
+    assert lib.mm4_gemm_workspace_size(h) == ((512 * 512 * 4 + 2 * 2 * 8 + 255) // 256) * 256
     lib.mm4_gemm_plan_destroy(h)
     rc, h = _gemm(M=33, N=40, K=31, transpose_right=1)
     assert rc == 0 and b"simt" in lib.mm4_gemm_plan_kernel_name(h)
