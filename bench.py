@@ -365,30 +365,39 @@ def build_gemm(w, dist, dev, gen, l2):
     P, r = dist.world, dist.rank
     M, N, K = w.M, w.N, w.K
     if P > 1 and w.split > 1:
-        # K shards of one problem + fp32 NCCL reduce to rank 0 + bias/cast there.
-        from example_matmul_metal4_b200.parallel import k_shard, reduce_partials, splitk_per_rank
-        k0, k1 = k_shard(K, P, r)
-        full = w.inputs(dev, gen)  # identical on every rank (same seed)
-        A = full["A"][:, k0:k1].contiguous()
-        B = full["B"][k0:k1].contiguous()
-        bias = full["bias"]
-        del full
+        # One K shard per rank of a global problem with K * P (the BASELINE K per rank: weak scaling);
+        # the shards' fp32 partials meet inside the split-K kernels over peer memory (SplitKGroup):
+        # one launch per GPU per step, no separate collective; the root's C holds the result.
+        import torch.distributed as tdist
+        from example_matmul_metal4_b200.parallel import SplitKGroup
+        t = w.inputs(dev, gen)  # this rank's shard (per-rank seed)
+        A, B = t["A"], t["B"]
+        bias = t["bias"]
+        tdist.broadcast(bias, src=0)  # one bias for the whole problem
+        plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
+                        buildOptions=BuildOptions(splitK=w.split))
+        grp = SplitKGroup(plan, root=0)
+        ws = plan.workspace(dev)
         sets = input_sets({"A": A, "B": B}, l2)
         nxt = cycling(sets)
-        plan = GemmPlan(GEMMDimensions(M, N, k1 - k0), transpose=(False, False), bias=False,
-                        buildOptions=BuildOptions(splitK=splitk_per_rank(w.split, P)))
-        C32 = torch.empty((M, N), dtype=torch.float32, device=dev)
-        C = torch.empty((M, N), dtype=torch.float16, device=dev)
-        ws = plan.workspace(dev)
 
         def step():
             t = nxt()
-            plan.partial(t["A"], t["B"], C32=C32, workspace=ws)
-            reduce_partials(C32, dst=0)
+            grp.run(t["A"], t["B"], bias, workspace=ws)
+        step.close = grp.close
+
+        hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
+        hC = torch.empty((M, N), dtype=torch.float16).pin_memory() if r == 0 else None
+
+        def e2e_step():
+            A.copy_(hA, non_blocking=True)
+            B.copy_(hB, non_blocking=True)
+            grp.run(A, B, bias, workspace=ws)
             if r == 0:
-                splitk_finalize(C32, bias, C=C)
-        return (step, None, None, plan.kernel_name + " + nccl reduce + finalize", (2 if r == 0 else 1), "strong",
-                len(sets))
+                hC.copy_(grp.C, non_blocking=True)
+        e2e_bytes = (A.numel() * 2 + B.numel() * 2, M * N * 2 if r == 0 else 0)
+        return (step, e2e_step, e2e_bytes, plan.kernel_name + " + in-kernel cross-GPU reduce over peer memory", 1,
+                "weak", len(sets))
     t = w.inputs(dev, gen)
     A, B, bias = t["A"], t["B"], t["bias"]
     sets = input_sets({"A": A, "B": B}, l2)
@@ -482,8 +491,7 @@ def run_mm4(args, w, dist, peaks):
     dist.init("nccl")
     stream = torch.cuda.current_stream()
     gen = torch.Generator(device=dev)
-    same_inputs = isinstance(w, GemmWorkload) and w.split > 1
-    gen.manual_seed(w.seed * 1000003 + (0 if same_inputs else dist.rank))
+    gen.manual_seed(w.seed * 1000003 + dist.rank)
     builder = (build_gemm if isinstance(w, GemmWorkload) else
                build_attention if isinstance(w, AttentionWorkload) else build_conv)
     step, e2e_step, e2e_bytes, kernel_name, launches, scaling, nsets = builder(w, dist, dev, gen, args.l2)
@@ -511,6 +519,8 @@ def run_mm4(args, w, dist, peaks):
         e2e_ms = dist.max(sum(time_steps(e2e_step, n_e2e, 2, flush, stream, dist)) / n_e2e)
         e2e = {"value": units * w.flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(e2e_bytes[0]), "d2h_bytes_per_step": int(e2e_bytes[1])}
+    if hasattr(step, "close"):
+        step.close()  # collective on every rank (peer mappings, exchange buffers)
 
     roof = None
     if dist.world == 1:
@@ -652,9 +662,14 @@ def main():
             cpu = cpu_sample(w, seconds_hint=args.cpu_seconds)
         cfg["kernel"] = res["kernel"]
         cfg["l2"] = cfg["l2"].replace("{n}", str(res["nsets"]))
-        cfg["parallelism"] = ("single GPU" if args.gpus == 1 else
-                              ("K-shard + NCCL fp32 reduce" if res["scaling"] == "strong" else
-                               f"{args.gpus} independent shards, no collective"))
+        if args.gpus == 1:
+            cfg["parallelism"] = "single GPU"
+        elif isinstance(w, GemmWorkload) and w.split > 1:
+            cfg["parallelism"] = (f"{args.gpus} K shards of a global K = {w.K} x {args.gpus} (rank r owns K rows "
+                                  f"[{w.K}r, {w.K}(r+1))), fp32 partials summed inside the split-K kernels over "
+                                  "peer memory (NVLink) into rank 0's C; one launch per GPU per step")
+        else:
+            cfg["parallelism"] = f"{args.gpus} independent shards, no collective"
         line = dict(base, value=res["value"], ms_per_step=res["ms"], scaling=res["scaling"], config=cfg,
                     pct_of_measured_bf16_peak=res["value"] / args.gpus / peaks["bf16_tflops"],
                     clocks=res["clocks"], e2e=res["e2e"], roofline=res["roofline"], cpu_baseline=cpu,

@@ -60,6 +60,11 @@ class Conv3dDesc(ctypes.Structure):
         "padding_right", "padding_front", "padding_back", "weight_layout", "bias")]
 
 
+class PeerHandle(ctypes.Structure):
+    """mm4_peer_handle: a CUDA IPC memory handle as plain bytes."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _sz = ctypes.c_size_t
@@ -83,6 +88,15 @@ SIGNATURES = {
     "mm4_gemm_partial_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mm4_splitk_finalize": (ctypes.c_int, [_i32, _i32, _vp, _vp, _vp, _vp]),
     "mm4_gemm_splitk_run_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "mm4_peer_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_vp), ctypes.POINTER(PeerHandle)]),
+    "mm4_peer_free": (ctypes.c_int, [_vp]),
+    "mm4_peer_open": (ctypes.c_int, [ctypes.POINTER(PeerHandle), ctypes.POINTER(_vp)]),
+    "mm4_peer_close": (ctypes.c_int, [_vp]),
+    "mm4_splitk_group_exchange_bytes": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_sz)]),
+    "mm4_splitk_group_create": (ctypes.c_int, [ctypes.POINTER(_vp), _vp, _i32, _i32, _i32, ctypes.POINTER(_vp),
+                                               _vp]),
+    "mm4_splitk_group_destroy": (None, [_vp]),
+    "mm4_gemm_splitk_group_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mm4_attention_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(AttentionDesc)]),
     "mm4_attention_plan_destroy": (None, [_vp]),
     "mm4_attention_plan_kernel_name": (ctypes.c_char_p, [_vp]),

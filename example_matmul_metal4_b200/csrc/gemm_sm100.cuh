@@ -40,6 +40,30 @@ enum GemmMode : int {
   MODE_SPLITK_F32 = 3,  // splits > 1: workspace reduce, fp32 output, no bias
 };
 
+// Multi-GPU split-K: each rank runs the same plan on its own K shard; the
+// ranks' fp32 partials meet in the epilogue over peer memory (one kernel per
+// GPU, no separate collective). Every finalize slice (a 128-row half tile x
+// one split's row range) has an owner rank (slice % world). The CTA that
+// finalizes a slice locally stores its fp32 rows into the owner's staging
+// block for this source rank and raises a flag there; the owner's CTA for the
+// slice waits for all ranks' flags, sums the partials in rank order, adds
+// bias, rounds, writes the rows into the root's C and counts the slice done on
+// the root; the root's kernel ends once every slice is done. Staging and flags
+// alternate between two halves by run parity (a rank cannot run two launches
+// ahead of another: every rank owns a slice and waits for all ranks in it).
+constexpr int MM4_MAX_GROUP = 8;
+struct SplitKGroupArgs {
+  int world;                     // ranks (<= 1: single GPU)
+  int rank, root;
+  int num_slices;                // half tiles x splits
+  unsigned long long epoch;      // run index, the same on every rank
+  long long stage_rows;          // rows of one source's staging block
+  float* stage[MM4_MAX_GROUP];   // owner r: [2][world][stage_rows][ws_ld] fp32 (peer-mapped)
+  unsigned long long* flags[MM4_MAX_GROUP];  // owner r: [2][num_slices][world] (peer-mapped)
+  unsigned long long* done;      // root: [num_slices], run tag once the slice's C rows are written (peer-mapped)
+  __half* c_root;                // root's C [M][N] fp16 (peer-mapped)
+};
+
 struct GemmArgs {
   int M, N, K;
   int num_m_tiles, num_n_tiles, num_tiles;
@@ -59,6 +83,7 @@ struct GemmArgs {
   int rm_tw, rm_th, rm_tiles_w, rm_tiles_h, rm_od, rm_oh, rm_ow;
   int* status;
   unsigned long long timeout_ns;
+  SplitKGroupArgs grp;    // multi-GPU split-K (grp.world > 1), cooperative finalize only
 };
 
 constexpr int GEMM_BM = 128;
@@ -95,6 +120,8 @@ enum : int {
   SITE_GEMM_MMA_DRAIN = 5,
   SITE_GEMM_EPI_TMEM_FULL = 6,
   SITE_GEMM_EPI_TILE_RENDEZVOUS = 7,
+  SITE_GEMM_GROUP_FLAGS = 8,
+  SITE_GEMM_GROUP_DONE = 9,
 };
 
 struct GemmUnit {
@@ -129,6 +156,92 @@ __device__ __forceinline__ GemmUnit gemm_decode_unit(const GemmArgs& a, int u) {
   w.kb0 = static_cast<int>((static_cast<long long>(w.split) * a.kb_total) / a.splits);
   w.kb1 = static_cast<int>((static_cast<long long>(w.split + 1) * a.kb_total) / a.splits);
   return w;
+}
+
+// Multi-GPU split-K finalize of one slice (see SplitKGroupArgs), run by the
+// 128 epilogue threads of the CTA that finalizes the slice on this rank.
+template <int BN>
+__device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_tile, int split, int row_base,
+                                               int col0, int r_begin, int r_end, int ethread, volatile int* s_last,
+                                               const Watchdog& wd) {
+  const SplitKGroupArgs& g = args.grp;
+  const int slice = ctr_tile * args.splits + split;
+  const int owner = slice % g.world;
+  const int parity = static_cast<int>(g.epoch & 1ull);
+  const unsigned long long tag = g.epoch + 1ull;
+  constexpr int TPR = BN / 4;     // threads per row (float4 each)
+  constexpr int RPI = 128 / TPR;  // rows per iteration
+  const int tr = ethread / TPR;
+  const int gc = col0 + (ethread % TPR) * 4;
+  const size_t block = static_cast<size_t>(g.stage_rows) * args.ws_ld;  // one source rank's staging block
+  // 1. This rank's fp32 rows of the slice go to the owner's staging block for
+  //    this rank (peer stores over NVLink, or local); the local workspace rows
+  //    are re-zeroed for the next launch.
+  float* dst = g.stage[owner] + (static_cast<size_t>(parity) * g.world + g.rank) * block;
+  for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
+    float4 v[4];  // up to four rows in flight: loads first, then the stores
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int rr = rr0 + b * RPI;
+      if (rr < r_end) v[b] = __ldcg(reinterpret_cast<const float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int rr = rr0 + b * RPI;
+      if (rr >= r_end) break;
+      const size_t off = static_cast<size_t>(row_base + rr) * args.ws_ld + gc;
+      __stcg(reinterpret_cast<float4*>(args.ws + off), make_float4(0.f, 0.f, 0.f, 0.f));
+      __stcg(reinterpret_cast<float4*>(dst + off), v[b]);
+    }
+  }
+  // The CTA barrier orders every thread's stores before thread 0's
+  // system-scope release (release is cumulative).
+  named_barrier(1, 128);
+  unsigned long long* flags = g.flags[owner] + (static_cast<size_t>(parity) * g.num_slices + slice) * g.world;
+  if (ethread == 0) st_release_sys_u64(flags + g.rank, tag);
+  if (owner != g.rank) return;
+  // 2. Owner: wait for every rank's rows, sum them in rank order, add bias,
+  //    round to fp16 and store into the root's C.
+  // One thread per source rank polls its flag.
+  const bool ok = ethread >= g.world || wait_all_ge_sys_u64(flags + ethread, 1, tag, wd, SITE_GEMM_GROUP_FLAGS);
+  if (!named_barrier_and(1, 128, ok)) return;
+  float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+  if (args.bias != nullptr) {
+    if (gc + 0 < args.N) b0 = __half2float(args.bias[gc + 0]);
+    if (gc + 1 < args.N) b1 = __half2float(args.bias[gc + 1]);
+    if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
+    if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
+  }
+  const float* own = g.stage[g.rank] + static_cast<size_t>(parity) * g.world * block;
+  const bool vec = (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(g.c_root) & 7u) == 0;
+  for (int rr = r_begin + tr; rr < r_end; rr += RPI) {
+    const int grow = row_base + rr;
+    const size_t off = static_cast<size_t>(grow) * args.ws_ld + gc;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(own + off));
+    for (int src = 1; src < g.world; ++src) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(own + src * block + off));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if (grow >= args.M) continue;
+    __half* c = g.c_root + static_cast<size_t>(grow) * args.N + gc;
+    const float o0 = acc.x + b0, o1 = acc.y + b1, o2 = acc.z + b2, o3 = acc.w + b3;
+    if (vec && gc + 4 <= args.N) {
+      uint2 pk;
+      pk.x = pack_half2(o0, o1);
+      pk.y = pack_half2(o2, o3);
+      *reinterpret_cast<uint2*>(c) = pk;
+    } else {
+      if (gc + 0 < args.N) c[0] = __float2half_rn(o0);
+      if (gc + 1 < args.N) c[1] = __float2half_rn(o1);
+      if (gc + 2 < args.N) c[2] = __float2half_rn(o2);
+      if (gc + 3 < args.N) c[3] = __float2half_rn(o3);
+    }
+  }
+  named_barrier(1, 128);
+  if (ethread == 0) st_release_sys_u64(g.done + slice, tag);
 }
 
 // All four epilogue warps agree on whether to proceed (every thread reaches
@@ -375,6 +488,14 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
           r_end = GEMM_BM;
         }
       }
+      if (args.grp.world > 1) {
+        // Multi-GPU: the rank-local sum of this slice joins the other ranks'.
+        if (*s_last) {
+          __threadfence();
+          group_finalize<BN>(args, ctr_tile, w.split, row_base, col0, r_begin, r_end, ethread, s_last, wd);
+        }
+        r_end = r_begin;
+      }
       if (r_end > r_begin) {
         __threadfence();
         // Sum is complete: add bias, round, store; re-zero the workspace rows.
@@ -439,6 +560,19 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       }
     }
     ++tiles_done;
+  }
+  if constexpr (SPLITK) {
+    // Multi-GPU root: the launch ends only once every slice of C is written.
+    // Spread over every epilogue thread of every root CTA, one flag each.
+    if (args.grp.world > 1 && args.grp.rank == args.grp.root) {
+      const int stride = static_cast<int>(gridDim.x) * 128;
+      for (int sl = static_cast<int>(blockIdx.x) + ethread * static_cast<int>(gridDim.x); sl < args.grp.num_slices;
+           sl += stride) {
+        if (aborted(wd.status) ||
+            !wait_all_ge_sys_u64(args.grp.done + sl, 1, args.grp.epoch + 1ull, wd, SITE_GEMM_GROUP_DONE))
+          break;
+      }
+    }
   }
 }
 

@@ -67,8 +67,14 @@ bool cooperative_finalize_enabled() {
   return on;
 }
 
-mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const void* bias, void* C, float* C32,
-                  void* ws, size_t ws_bytes, cudaStream_t st) {
+}  // namespace
+
+namespace mm4 {
+
+// Tensor-core launch shared by the entry points; `grp` (may be null) joins a
+// multi-GPU split-K group, which needs the cooperative finalize.
+mm4_status gemm_run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const void* bias, void* C, float* C32,
+                       void* ws, size_t ws_bytes, cudaStream_t st, const SplitKGroupArgs* grp) {
   DeviceInfo info;
   mm4_status rc = current_device(&info);
   if (rc != MM4_OK) return rc;
@@ -107,8 +113,22 @@ mm4_status run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const vo
   } else {
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
   }
+  if (grp && grp->world > 1) {
+    if (p->splits < 2 || out_f32)
+      return fail(MM4_ERR_UNSUPPORTED, "a multi-GPU split-K group needs a split-K plan (split_k >= 2)");
+    if (!args.coop_finalize)
+      return fail(MM4_ERR_UNSUPPORTED,
+                  "a multi-GPU split-K group needs one CTA (pair) per (split, M-tile) resident at once: %d x %d "
+                  "%s does not fit this device's %d SMs (or MM4_SPLITK_COOPERATIVE=0)",
+                  p->splits, p->num_m_tiles, p->pair ? "CTA pairs" : "CTAs", info.sm_count);
+    args.grp = *grp;
+  }
   return gemm_dispatch(p, mode, ta, tb, args, gemm_grid(p, args.num_units, info.sm_count), st);
 }
+
+}  // namespace mm4
+
+namespace {
 
 mm4_status validate(const mm4_gemm_desc* d) {
   if (!d) return fail(MM4_ERR_INVALID, "null gemm descriptor");
@@ -211,7 +231,7 @@ mm4_status mm4_gemm_run(const mm4_gemm_plan* p, const void* A, const void* B, co
   for (int i = 0; i < duplicated_count; ++i) {
     mm4_status rc;
     if (tc) {
-      rc = run_tc(p, A, B, bias, C, nullptr, workspace, workspace_bytes, st);
+      rc = gemm_run_tc(p, A, B, bias, C, nullptr, workspace, workspace_bytes, st);
     } else {
       DeviceInfo info;
       rc = current_device(&info);
@@ -228,7 +248,7 @@ mm4_status mm4_gemm_partial_run(const mm4_gemm_plan* p, const void* A, const voi
   if (!A || !B || !C32) return fail(MM4_ERR_INVALID, "null A/B/C32 pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->tensor_core && aligned16(A) && aligned16(B))
-    return run_tc(p, A, B, nullptr, nullptr, C32, workspace, workspace_bytes, st);
+    return gemm_run_tc(p, A, B, nullptr, nullptr, C32, workspace, workspace_bytes, st);
   DeviceInfo info;
   mm4_status rc = current_device(&info);
   if (rc != MM4_OK) return rc;

@@ -3,6 +3,8 @@
 
 #include <cstddef>
 
+#include <cuda_runtime.h>
+
 #include "mm4.h"
 
 struct mm4_gemm_plan {
@@ -17,3 +19,11 @@ struct mm4_gemm_plan {
   size_t ws_counter_offset;
   char name[96];
 };
+
+namespace mm4 {
+struct SplitKGroupArgs;
+// Tensor-core GEMM launch (mm4_gemm.cu): fp16 C with bias, or fp32 C32 partial
+// when C32 is set; `grp` joins a multi-GPU split-K group.
+mm4_status gemm_run_tc(const mm4_gemm_plan* p, const void* A, const void* B, const void* bias, void* C, float* C32,
+                       void* ws, size_t ws_bytes, cudaStream_t st, const SplitKGroupArgs* grp = nullptr);
+}  // namespace mm4

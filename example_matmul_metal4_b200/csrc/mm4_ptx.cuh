@@ -132,6 +132,20 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over the participating threads.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(nthreads)
+      : "memory");
+  return out != 0;
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -414,6 +428,38 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
       "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+
+// System-scope release/acquire on 64-bit words that may live in another
+// GPU's memory (peer-mapped over NVLink).
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Bounded wait until all n words p[0..n) are >= target (system scope), polled
+// with relaxed loads and closed by one acquire fence. Returns false, with the
+// error recorded, when the limit runs out or another role aborted.
+__device__ __forceinline__ bool wait_all_ge_sys_u64(const unsigned long long* p, int n, unsigned long long target,
+                                                    const Watchdog& wd, int site) {
+  const uint64_t t0 = globaltimer_ns();
+  int first = 0;  // words before `first` are known to be ready
+  while (true) {
+    while (first < n && ld_relaxed_sys_u64(p + first) >= target) ++first;
+    if (first == n) break;
+    if (aborted(wd.status) || globaltimer_ns() - t0 > wd.limit_ns) {
+      record_error(wd.status, MM4_ERR_TIMEOUT, site);
+      return false;
+    }
+  }
+  fence_acq_rel_sys();
+  return true;
 }
 
 // Per-warpgroup register budget (setmaxnreg). The four warps of a warpgroup

@@ -80,3 +80,107 @@ class StepHeartbeat:
             if time.monotonic() > deadline:
                 raise RankLost(step, waiting)
             time.sleep(0.002)
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ over a raw device pointer (for a zero-copy torch view)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "strides": None, "version": 3}
+
+
+class SplitKGroup:
+    """Fused multi-GPU split-K GEMM (mm4_gemm_splitk_group_run): every rank runs `plan` on its own K
+    shard and the ranks' fp32 partials are summed inside the kernels over peer memory (CUDA IPC
+    mappings over NVLink) into the root's C: one launch per GPU, no separate collective.
+
+    Construction is collective (every rank of the default process group, same plan shape): each rank
+    allocates its exchange buffer, the root also its C, and the handles are exchanged with
+    all_gather_object / broadcast_object_list. `C` is the root's [M][N] fp16 output (None elsewhere);
+    after `run` returns on the root's stream, the root's later work on that stream sees all of C.
+    Every rank must call `run` the same number of times. Call `close()` on every rank when done."""
+
+    def __init__(self, plan, root: int = 0):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+        L = _lib.lib()
+        self._L, self._lib, self.plan, self.root = L, _lib, plan, root
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        M, N = plan.dims.M, plan.dims.N
+        nbytes = ctypes.c_size_t()
+        _lib.check(L.mm4_splitk_group_exchange_bytes(plan._h, self.world, ctypes.byref(nbytes)))
+        self._own, self._c_own, self._opened, self._g = ctypes.c_void_p(), None, [], None
+        h, hc = _lib.PeerHandle(), _lib.PeerHandle()
+        _lib.check(L.mm4_peer_alloc(nbytes.value, ctypes.byref(self._own), ctypes.byref(h)))
+        if self.rank == root:
+            self._c_own = ctypes.c_void_p()
+            _lib.check(L.mm4_peer_alloc(M * N * 2, ctypes.byref(self._c_own), ctypes.byref(hc)))
+        handles = [bytes(h.bytes)]
+        c_handle = bytes(hc.bytes)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h.bytes))
+            obj = [c_handle if self.rank == root else None]
+            dist.broadcast_object_list(obj, src=root)
+            c_handle = obj[0]
+        ptrs = (ctypes.c_void_p * self.world)()
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs[r] = self._own.value
+            else:
+                ptrs[r] = self._open(handles[r]).value
+        c_root = self._c_own if self.rank == root else self._open(c_handle)
+        g = ctypes.c_void_p()
+        _lib.check(L.mm4_splitk_group_create(ctypes.byref(g), plan._h, self.world, self.rank, root, ptrs, c_root))
+        self._g = g
+        self.C = None
+        if self.rank == root:
+            self.C = torch.as_tensor(_DeviceArray(self._c_own.value, (M, N), "<f2"), device="cuda")
+
+    def _open(self, handle_bytes):
+        import ctypes
+        ph = self._lib.PeerHandle.from_buffer_copy(handle_bytes)
+        p = ctypes.c_void_p()
+        self._lib.check(self._L.mm4_peer_open(ctypes.byref(ph), ctypes.byref(p)))
+        self._opened.append(p)
+        return p
+
+    def run(self, A, B, bias=None, workspace=None, stream=None):
+        """One fused step: this rank's K shard (A [M][K_r], B [K_r][N], fp16) into the root's C."""
+        from .gemm import _check_tensor
+        _check_tensor(A, self.plan.a_shape(), "A")
+        _check_tensor(B, self.plan.b_shape(), "B")
+        if self.plan.bias:
+            _check_tensor(bias, (self.plan.dims.N,), "bias")
+        ws = workspace if workspace is not None else self.plan.workspace(A.device)
+        self._lib.check(self._L.mm4_gemm_splitk_group_run(
+            self.plan._h, self._g, A.data_ptr(), B.data_ptr(), bias.data_ptr() if self.plan.bias else None,
+            ws.data_ptr(), ws.numel(), self._lib.stream_handle(stream)))
+        return self.C
+
+    def close(self):
+        """Collective: releases the group, the peer mappings and this rank's buffers."""
+        import torch
+        import torch.distributed as dist
+        if self._g is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier()  # no rank still runs a kernel that maps our buffers
+        self._L.mm4_splitk_group_destroy(self._g)
+        self._g = None
+        self.C = None
+        for p in self._opened:
+            self._L.mm4_peer_close(p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier()  # every rank has unmapped before the owners free
+        self._L.mm4_peer_free(self._own)
+        if self._c_own is not None:
+            self._L.mm4_peer_free(self._c_own)

@@ -150,6 +150,48 @@ MM4_API mm4_status mm4_splitk_finalize(int32_t M, int32_t N, const float* C32, c
 MM4_API mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* plan, const void* A, const void* B,
                                                const void* bias, void* C, mm4_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU split-K: one process per GPU, fused compute + cross-GPU reduce  */
+/* ------------------------------------------------------------------------ */
+
+/* Device memory another process on this node can map (CUDA IPC), zero-filled.
+ * The handle is plain bytes to pass between processes (e.g. through
+ * torch.distributed.all_gather_object). No reference counterpart (the
+ * reference is single-device). */
+typedef struct mm4_peer_handle {
+  unsigned char bytes[64];
+} mm4_peer_handle;
+MM4_API mm4_status mm4_peer_alloc(size_t bytes, void** ptr, mm4_peer_handle* handle);
+MM4_API mm4_status mm4_peer_free(void* ptr);
+MM4_API mm4_status mm4_peer_open(const mm4_peer_handle* handle, void** ptr);
+MM4_API mm4_status mm4_peer_close(void* ptr);
+
+/* A group of `world` ranks (<= 8) running one split-K plan, each on its own K
+ * shard (same M, N, shard K, split_k on every rank), whose fp32 partials are
+ * summed inside the kernels over peer memory: the CTA that finalizes a slice
+ * of C on a rank stores its rows into the slice owner's exchange buffer, the
+ * owner sums the ranks' rows in rank order, adds bias, rounds to fp16 and
+ * writes them into the root's C. One launch per GPU and no separate
+ * collective; the root's launch completes when all of C is written. Replaces
+ * the NCCL reduce a multi-GPU port would put after the per-split partials of
+ * matmul.swift:127-185 + the bias/cast of :21-38.
+ *
+ * Every rank allocates an exchange buffer of mm4_splitk_group_exchange_bytes()
+ * with mm4_peer_alloc; the root also allocates C [M][N] fp16 with
+ * mm4_peer_alloc. exchange[r] is rank r's buffer as mapped in this process
+ * (mm4_peer_open; this rank's own pointer at [rank]); c_root likewise. Every
+ * rank must make the same sequence of mm4_gemm_splitk_group_run calls. The
+ * plan must give one CTA (pair) per (split, M-tile) on the device (split_k x
+ * M-tiles <= the SM count, or half of it for 256-row tiles). */
+typedef struct mm4_splitk_group mm4_splitk_group;
+MM4_API mm4_status mm4_splitk_group_exchange_bytes(const mm4_gemm_plan* plan, int32_t world, size_t* bytes);
+MM4_API mm4_status mm4_splitk_group_create(mm4_splitk_group** group, const mm4_gemm_plan* plan, int32_t world,
+                                           int32_t rank, int32_t root, void* const* exchange, void* c_root);
+MM4_API void mm4_splitk_group_destroy(mm4_splitk_group* group);
+MM4_API mm4_status mm4_gemm_splitk_group_run(const mm4_gemm_plan* plan, mm4_splitk_group* group, const void* A,
+                                             const void* B, const void* bias, void* workspace,
+                                             size_t workspace_bytes, mm4_stream_t stream);
+
 /* ======================================================================== */
 /* Flash-attention forward                                                  */
 /* ======================================================================== */
