@@ -377,13 +377,12 @@ def build_gemm(w, dist, dev, gen, l2):
         plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
                         buildOptions=BuildOptions(splitK=w.split))
         grp = SplitKGroup(plan, root=0)
-        ws = plan.workspace(dev)
         sets = input_sets({"A": A, "B": B}, l2)
         nxt = cycling(sets)
 
         def step():
             t = nxt()
-            grp.run(t["A"], t["B"], bias, workspace=ws)
+            grp.run(t["A"], t["B"], bias)
         step.close = grp.close
 
         hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
@@ -392,7 +391,7 @@ def build_gemm(w, dist, dev, gen, l2):
         def e2e_step():
             A.copy_(hA, non_blocking=True)
             B.copy_(hB, non_blocking=True)
-            grp.run(A, B, bias, workspace=ws)
+            grp.run(A, B, bias)
             if r == 0:
                 hC.copy_(grp.C, non_blocking=True)
         e2e_bytes = (A.numel() * 2 + B.numel() * 2, M * N * 2 if r == 0 else 0)

@@ -96,7 +96,7 @@ SIGNATURES = {
     "mm4_splitk_group_create": (ctypes.c_int, [ctypes.POINTER(_vp), _vp, _i32, _i32, _i32, ctypes.POINTER(_vp),
                                                _vp]),
     "mm4_splitk_group_destroy": (None, [_vp]),
-    "mm4_gemm_splitk_group_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "mm4_gemm_splitk_group_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "mm4_attention_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(AttentionDesc)]),
     "mm4_attention_plan_destroy": (None, [_vp]),
     "mm4_attention_plan_kernel_name": (ctypes.c_char_p, [_vp]),

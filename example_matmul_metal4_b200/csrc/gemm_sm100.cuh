@@ -42,27 +42,40 @@ enum GemmMode : int {
 
 // Multi-GPU split-K: each rank runs the same plan on its own K shard; the
 // ranks' fp32 partials meet in the epilogue over peer memory (one kernel per
-// GPU, no separate collective). Every finalize slice (a 128-row half tile x
-// one split's row range) has an owner rank (slice % world). The CTA that
-// finalizes a slice locally stores its fp32 rows into the owner's staging
-// block for this source rank and raises a flag there; the owner's CTA for the
-// slice waits for all ranks' flags, sums the partials in rank order, adds
-// bias, rounds, writes the rows into the root's C and counts the slice done on
-// the root; the root's kernel ends once every slice is done. Staging and flags
-// alternate between two halves by run parity (a rank cannot run two launches
-// ahead of another: every rank owns a slice and waits for all ranks in it).
+// GPU, no separate collective). The split-K scratch stays rank-local; each
+// rank publishes finished slices (a 128-row half tile x one split's row
+// range) into a staging area of its exchange buffer, which every other rank
+// maps. Per slice:
+//   1. the CTA that completes the slice's rank-local sum copies the rows into
+//      its staging half for this run (two halves, by run parity), re-zeroes
+//      the scratch rows and raises ready[slice][rank] on the slice's owner
+//      (the root, or slice % world for groups of more than four);
+//   2. the owner's CTA for the slice waits for every rank's flag, reads the
+//      ranks' rows from their staging (peer loads), sums them in rank order,
+//      adds bias, rounds, stores the rows into the root's C and raises
+//      consumed[slice] on every rank (and done[slice] on the root when it is
+//      not the root itself);
+//   3. a rank overwrites a staging half (two runs later) only after the owner
+//      consumed it; the root's launch ends once every slice is in C.
+// Cross-GPU traffic is peer loads (and C stores) plus release/acquire flags
+// that carry the run index + 1 (no remote atomics, nothing to reset).
 constexpr int MM4_MAX_GROUP = 8;
 struct SplitKGroupArgs {
   int world;                     // ranks (<= 1: single GPU)
   int rank, root;
+  int owner_mode;                // 0: the root owns every slice; 1: slice % world
   int num_slices;                // half tiles x splits
   unsigned long long epoch;      // run index, the same on every rank
-  long long stage_rows;          // rows of one source's staging block
-  float* stage[MM4_MAX_GROUP];   // owner r: [2][world][stage_rows][ws_ld] fp32 (peer-mapped)
-  unsigned long long* flags[MM4_MAX_GROUP];  // owner r: [2][num_slices][world] (peer-mapped)
-  unsigned long long* done;      // root: [num_slices], run tag once the slice's C rows are written (peer-mapped)
+  float* stage[MM4_MAX_GROUP];   // rank r's staging half for this run [rows][ws_ld] fp32 (peer-mapped)
+  unsigned long long* ready[MM4_MAX_GROUP];     // rank r: [num_slices][world]
+  unsigned long long* consumed[MM4_MAX_GROUP];  // rank r: [num_slices]
+  unsigned long long* done;      // root: [num_slices]
   __half* c_root;                // root's C [M][N] fp16 (peer-mapped)
 };
+
+__device__ __forceinline__ int group_owner(const SplitKGroupArgs& g, int slice) {
+  return g.owner_mode == 0 ? g.root : slice % g.world;
+}
 
 struct GemmArgs {
   int M, N, K;
@@ -122,6 +135,7 @@ enum : int {
   SITE_GEMM_EPI_TILE_RENDEZVOUS = 7,
   SITE_GEMM_GROUP_FLAGS = 8,
   SITE_GEMM_GROUP_DONE = 9,
+  SITE_GEMM_GROUP_SCRATCH = 10,
 };
 
 struct GemmUnit {
@@ -159,27 +173,24 @@ __device__ __forceinline__ GemmUnit gemm_decode_unit(const GemmArgs& a, int u) {
 }
 
 // Multi-GPU split-K finalize of one slice (see SplitKGroupArgs), run by the
-// 128 epilogue threads of the CTA that finalizes the slice on this rank.
+// 128 epilogue threads of the CTA that completed the slice's rank-local sum.
 template <int BN>
 __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_tile, int split, int row_base,
-                                               int col0, int r_begin, int r_end, int ethread, volatile int* s_last,
-                                               const Watchdog& wd) {
+                                               int col0, int r_begin, int r_end, int ethread, const Watchdog& wd) {
   const SplitKGroupArgs& g = args.grp;
   const int slice = ctr_tile * args.splits + split;
-  const int owner = slice % g.world;
-  const int parity = static_cast<int>(g.epoch & 1ull);
+  const int owner = group_owner(g, slice);
   const unsigned long long tag = g.epoch + 1ull;
   constexpr int TPR = BN / 4;     // threads per row (float4 each)
   constexpr int RPI = 128 / TPR;  // rows per iteration
   const int tr = ethread / TPR;
   const int gc = col0 + (ethread % TPR) * 4;
-  const size_t block = static_cast<size_t>(g.stage_rows) * args.ws_ld;  // one source rank's staging block
-  // 1. This rank's fp32 rows of the slice go to the owner's staging block for
-  //    this rank (peer stores over NVLink, or local); the local workspace rows
-  //    are re-zeroed for the next launch.
-  float* dst = g.stage[owner] + (static_cast<size_t>(parity) * g.world + g.rank) * block;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  // 1. Publish (the staging half is free: group_unit_start checked it):
+  //    rows scratch -> staging, scratch re-zeroed, flag on the owner.
+  float* stage = g.stage[g.rank];
   for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
-    float4 v[4];  // up to four rows in flight: loads first, then the stores
+    float4 v[4];
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       const int rr = rr0 + b * RPI;
@@ -190,20 +201,19 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
       const int rr = rr0 + b * RPI;
       if (rr >= r_end) break;
       const size_t off = static_cast<size_t>(row_base + rr) * args.ws_ld + gc;
-      __stcg(reinterpret_cast<float4*>(args.ws + off), make_float4(0.f, 0.f, 0.f, 0.f));
-      __stcg(reinterpret_cast<float4*>(dst + off), v[b]);
+      __stcg(reinterpret_cast<float4*>(args.ws + off), zero);
+      __stcg(reinterpret_cast<float4*>(stage + off), v[b]);
     }
   }
-  // The CTA barrier orders every thread's stores before thread 0's
-  // system-scope release (release is cumulative).
-  named_barrier(1, 128);
-  unsigned long long* flags = g.flags[owner] + (static_cast<size_t>(parity) * g.num_slices + slice) * g.world;
-  if (ethread == 0) st_release_sys_u64(flags + g.rank, tag);
+  named_barrier(1, 128);  // orders every thread's stores before the release
+  if (ethread == 0) st_release_sys_u64(g.ready[owner] + static_cast<size_t>(slice) * g.world + g.rank, tag);
   if (owner != g.rank) return;
-  // 2. Owner: wait for every rank's rows, sum them in rank order, add bias,
-  //    round to fp16 and store into the root's C.
-  // One thread per source rank polls its flag.
-  const bool ok = ethread >= g.world || wait_all_ge_sys_u64(flags + ethread, 1, tag, wd, SITE_GEMM_GROUP_FLAGS);
+  // 2. Owner: one thread per rank polls that rank's flag; then every rank's
+  //    rows (peer loads, up to four rows per source in flight), summed in
+  //    rank order, bias, fp16 into the root's C.
+  const bool ok = ethread >= g.world ||
+                  wait_all_ge_sys_u64(g.ready[g.rank] + static_cast<size_t>(slice) * g.world + ethread, 1, tag, wd,
+                                      SITE_GEMM_GROUP_FLAGS);
   if (!named_barrier_and(1, 128, ok)) return;
   float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
   if (args.bias != nullptr) {
@@ -212,36 +222,78 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
     if (gc + 2 < args.N) b2 = __half2float(args.bias[gc + 2]);
     if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
   }
-  const float* own = g.stage[g.rank] + static_cast<size_t>(parity) * g.world * block;
   const bool vec = (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(g.c_root) & 7u) == 0;
-  for (int rr = r_begin + tr; rr < r_end; rr += RPI) {
-    const int grow = row_base + rr;
-    const size_t off = static_cast<size_t>(grow) * args.ws_ld + gc;
-    float4 acc = __ldcg(reinterpret_cast<const float4*>(own + off));
-    for (int src = 1; src < g.world; ++src) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(own + src * block + off));
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+  for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
+    float4 acc[4];
+#pragma unroll
+    for (int src = 0; src < MM4_MAX_GROUP; ++src) {
+      if (src >= g.world) break;
+      float4 v[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int rr = rr0 + b * RPI;
+        if (rr < r_end)
+          v[b] = __ldcg(reinterpret_cast<const float4*>(g.stage[src] + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+      }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        if (src == 0) {
+          acc[b] = v[b];
+        } else {
+          acc[b].x += v[b].x;
+          acc[b].y += v[b].y;
+          acc[b].z += v[b].z;
+          acc[b].w += v[b].w;
+        }
+      }
     }
-    if (grow >= args.M) continue;
-    __half* c = g.c_root + static_cast<size_t>(grow) * args.N + gc;
-    const float o0 = acc.x + b0, o1 = acc.y + b1, o2 = acc.z + b2, o3 = acc.w + b3;
-    if (vec && gc + 4 <= args.N) {
-      uint2 pk;
-      pk.x = pack_half2(o0, o1);
-      pk.y = pack_half2(o2, o3);
-      *reinterpret_cast<uint2*>(c) = pk;
-    } else {
-      if (gc + 0 < args.N) c[0] = __float2half_rn(o0);
-      if (gc + 1 < args.N) c[1] = __float2half_rn(o1);
-      if (gc + 2 < args.N) c[2] = __float2half_rn(o2);
-      if (gc + 3 < args.N) c[3] = __float2half_rn(o3);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int rr = rr0 + b * RPI;
+      const int grow = row_base + rr;
+      if (rr >= r_end || grow >= args.M) continue;
+      __half* c = g.c_root + static_cast<size_t>(grow) * args.N + gc;
+      const float o0 = acc[b].x + b0, o1 = acc[b].y + b1, o2 = acc[b].z + b2, o3 = acc[b].w + b3;
+      if (vec && gc + 4 <= args.N) {
+        uint2 pk;
+        pk.x = pack_half2(o0, o1);
+        pk.y = pack_half2(o2, o3);
+        *reinterpret_cast<uint2*>(c) = pk;
+      } else {
+        if (gc + 0 < args.N) c[0] = __float2half_rn(o0);
+        if (gc + 1 < args.N) c[1] = __float2half_rn(o1);
+        if (gc + 2 < args.N) c[2] = __float2half_rn(o2);
+        if (gc + 3 < args.N) c[3] = __float2half_rn(o3);
+      }
     }
   }
-  named_barrier(1, 128);
-  if (ethread == 0) st_release_sys_u64(g.done + slice, tag);
+  // 3. The root may finish once its C rows are in (the CTA barrier orders
+  //    every thread's stores before the release). The ranks learn that their
+  //    staging was consumed from the next launch (group_unit_start).
+  if (g.rank != g.root) {
+    named_barrier(1, 128);
+    if (ethread == 0) st_release_sys_u64(g.done + slice, tag);
+  }
+}
+
+// Multi-GPU split-K, at the start of a unit, while the epilogue warps wait for
+// the main loop (off the critical path):
+//   - the slice this CTA owned in the previous run was read by then (the
+//     launch boundary orders those loads): tell every rank it may reuse that
+//     staging half (consumed = previous run index + 1);
+//   - this CTA's staging half for this run was last written two runs ago:
+//     wait until its owner has consumed it.
+template <bool PAIR>
+__device__ __forceinline__ bool group_unit_start(const GemmArgs& args, const GemmUnit& w, uint32_t rank,
+                                                 int ethread, const Watchdog& wd) {
+  const SplitKGroupArgs& g = args.grp;
+  const int ct = PAIR ? 2 * w.tile + static_cast<int>(rank) : w.tile;
+  const int slice = ct * args.splits + w.split;
+  if (g.epoch >= 1 && group_owner(g, slice) == g.rank && ethread < g.world)
+    st_release_sys_u64(g.consumed[ethread] + slice, g.epoch);
+  const bool ok = g.epoch < 2 || ethread != 0 ||
+                  wait_all_ge_sys_u64(g.consumed[g.rank] + slice, 1, g.epoch - 1ull, wd, SITE_GEMM_GROUP_SCRATCH);
+  return named_barrier_and(1, 128, ok);
 }
 
 // All four epilogue warps agree on whether to proceed (every thread reaches
@@ -339,6 +391,9 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
     const GemmUnit w = gemm_decode_unit(args, u);
     const uint32_t acc = tiles_done % ACC_BUFS;
     const uint32_t aph = (tiles_done / ACC_BUFS) & 1u;
+    if constexpr (SPLITK) {
+      if (args.grp.world > 1 && !group_unit_start<PAIR>(args, w, rank, ethread, wd)) break;
+    }
     bool ok = mbar_wait(&tmem_full[acc], aph, wd, SITE_GEMM_EPI_TMEM_FULL);
     if (!epi_consensus(ok, q, lane, s_vote)) break;
     tc_fence_after();
@@ -492,7 +547,7 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
         // Multi-GPU: the rank-local sum of this slice joins the other ranks'.
         if (*s_last) {
           __threadfence();
-          group_finalize<BN>(args, ctr_tile, w.split, row_base, col0, r_begin, r_end, ethread, s_last, wd);
+          group_finalize<BN>(args, ctr_tile, w.split, row_base, col0, r_begin, r_end, ethread, wd);
         }
         r_end = r_begin;
       }
@@ -563,11 +618,13 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
   }
   if constexpr (SPLITK) {
     // Multi-GPU root: the launch ends only once every slice of C is written.
-    // Spread over every epilogue thread of every root CTA, one flag each.
-    if (args.grp.world > 1 && args.grp.rank == args.grp.root) {
+    // Slices other ranks own; spread over every epilogue thread of every root
+    // CTA, one flag each.
+    if (args.grp.world > 1 && args.grp.rank == args.grp.root && args.grp.owner_mode != 0) {
       const int stride = static_cast<int>(gridDim.x) * 128;
       for (int sl = static_cast<int>(blockIdx.x) + ethread * static_cast<int>(gridDim.x); sl < args.grp.num_slices;
            sl += stride) {
+        if (group_owner(args.grp, sl) == args.grp.rank) continue;
         if (aborted(wd.status) ||
             !wait_all_ge_sys_u64(args.grp.done + sl, 1, args.grp.epoch + 1ull, wd, SITE_GEMM_GROUP_DONE))
           break;

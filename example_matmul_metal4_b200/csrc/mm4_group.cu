@@ -5,6 +5,7 @@
 // launch per GPU with no separate collective. The reference is single-device;
 // this replaces the NCCL reduce of the K-shard partials a multi-GPU port would
 // place after the per-split partial of matmul.swift:127-185.
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -17,39 +18,42 @@ using namespace mm4;
 static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(mm4_peer_handle), "IPC handle does not fit mm4_peer_handle");
 
 struct mm4_splitk_group {
-  int world, rank, root;
+  int world, rank, root, owner_mode;
   int num_slices;
-  long long stage_rows;
-  int ws_ld;
+  size_t half_bytes;  // one staging half
   unsigned long long epoch;
-  float* stage[MM4_MAX_GROUP];
-  unsigned long long* flags[MM4_MAX_GROUP];
+  char* exchange[MM4_MAX_GROUP];
+  unsigned long long* ready[MM4_MAX_GROUP];
+  unsigned long long* consumed[MM4_MAX_GROUP];
   unsigned long long* done;
   __half* c_root;
+  void* scratch;      // rank-local split-K scratch (the plan's workspace), owned by the group
+  int device;
   // plan geometry the group was sized for
   int M, N, splits, num_tiles, halves;
+  size_t ws_bytes;
 };
 
 namespace {
 
-// Exchange buffer of one rank: [flags: 2][num_slices][world] u64 |
-// done: [num_slices] u64 (used on the root) | pad to 256 |
-// staging: [2][world][stage_rows][ws_ld] fp32.
+// Exchange buffer of one rank: staging half 0 | half 1 (each [stage_rows]
+// [ws_ld] fp32, 256-aligned) | ready [num_slices][world] u64 |
+// consumed [num_slices] u64 | done [num_slices] u64 (used on the root).
 struct ExchangeLayout {
-  size_t flags_bytes, done_offset, stage_offset, total;
+  size_t half_bytes, ready_offset, consumed_offset, done_offset, total;
 };
 
 ExchangeLayout exchange_layout(const mm4_gemm_plan* p, int world) {
   ExchangeLayout L;
   const int halves = p->pair ? 2 : 1;
   const size_t num_slices = static_cast<size_t>(p->num_tiles) * halves * p->splits;
-  L.flags_bytes = 2 * num_slices * world * sizeof(unsigned long long);
-  L.done_offset = L.flags_bytes;
-  L.stage_offset = (L.done_offset + num_slices * sizeof(unsigned long long) + 255) & ~static_cast<size_t>(255);
-  const size_t tile_m = p->pair ? 256 : 128;
-  const size_t stage_rows = static_cast<size_t>(p->num_m_tiles) * tile_m;
+  const size_t stage_rows = static_cast<size_t>(p->num_m_tiles) * (p->pair ? 256 : 128);
   const size_t ws_ld = static_cast<size_t>(p->num_n_tiles) * p->bn;
-  L.total = L.stage_offset + 2 * static_cast<size_t>(world) * stage_rows * ws_ld * sizeof(float);
+  L.half_bytes = (stage_rows * ws_ld * sizeof(float) + 255) & ~static_cast<size_t>(255);
+  L.ready_offset = 2 * L.half_bytes;
+  L.consumed_offset = L.ready_offset + num_slices * world * sizeof(unsigned long long);
+  L.done_offset = L.consumed_offset + num_slices * sizeof(unsigned long long);
+  L.total = L.done_offset + num_slices * sizeof(unsigned long long);
   return L;
 }
 
@@ -60,6 +64,17 @@ mm4_status check_group_plan(const mm4_gemm_plan* p, int world) {
   if (!p->tensor_core || p->splits < 2)
     return fail(MM4_ERR_UNSUPPORTED, "a split-K group needs a tensor-core split-K plan (got %s)", p->name);
   return MM4_OK;
+}
+
+// Which ranks finish the slices: the root alone for small groups (one hop,
+// the root reads (world-1) partials over NVLink), spread over all ranks for
+// larger ones (each rank reads (world-1)/world of a partial per slice it owns,
+// plus one hop to the root's C). MM4_SPLITK_GROUP_OWNERS=root|spread forces it.
+int choose_owner_mode(int world) {
+  const char* v = std::getenv("MM4_SPLITK_GROUP_OWNERS");
+  if (v && std::strcmp(v, "root") == 0) return 0;
+  if (v && std::strcmp(v, "spread") == 0) return 1;
+  return world <= 4 ? 0 : 1;
 }
 
 }  // namespace
@@ -126,22 +141,34 @@ mm4_status mm4_splitk_group_create(mm4_splitk_group** out, const mm4_gemm_plan* 
   if (!exchange || !c_root) return fail(MM4_ERR_INVALID, "null exchange buffers or root output");
   if ((reinterpret_cast<uintptr_t>(c_root) & 7u) != 0) return fail(MM4_ERR_INVALID, "root C must be 8-byte aligned");
   for (int r = 0; r < world; ++r)
-    if (!exchange[r] || !aligned16(exchange[r])) return fail(MM4_ERR_INVALID, "exchange[%d] null or unaligned", r);
+    if (!exchange[r] || (reinterpret_cast<uintptr_t>(exchange[r]) & 255u) != 0)
+      return fail(MM4_ERR_INVALID, "exchange[%d] null or not 256-byte aligned", r);
   mm4_splitk_group* g = new (std::nothrow) mm4_splitk_group();
   if (!g) return fail(MM4_ERR_INVALID, "out of host memory");
+  // Rank-local split-K scratch: plain device memory (the partial sums are
+  // reduced into it with L2 atomics; only finished slices are shared).
+  cudaError_t e = cudaGetDevice(&g->device);
+  if (e == cudaSuccess) e = cudaMalloc(&g->scratch, plan->ws_bytes);
+  if (e == cudaSuccess) e = cudaMemset(g->scratch, 0, plan->ws_bytes);
+  if (e != cudaSuccess) {
+    if (g->scratch) cudaFree(g->scratch);
+    delete g;
+    return cuda_fail(e, "split-K group scratch");
+  }
   const ExchangeLayout L = exchange_layout(plan, world);
   g->world = world;
   g->rank = rank;
   g->root = root;
+  g->owner_mode = choose_owner_mode(world);
   g->halves = plan->pair ? 2 : 1;
   g->num_slices = plan->num_tiles * g->halves * plan->splits;
-  g->stage_rows = static_cast<long long>(plan->num_m_tiles) * (plan->pair ? 256 : 128);
-  g->ws_ld = plan->num_n_tiles * plan->bn;
+  g->half_bytes = L.half_bytes;
   g->epoch = 0;
   for (int r = 0; r < world; ++r) {
     char* base = static_cast<char*>(exchange[r]);
-    g->flags[r] = reinterpret_cast<unsigned long long*>(base);
-    g->stage[r] = reinterpret_cast<float*>(base + L.stage_offset);
+    g->exchange[r] = base;
+    g->ready[r] = reinterpret_cast<unsigned long long*>(base + L.ready_offset);
+    g->consumed[r] = reinterpret_cast<unsigned long long*>(base + L.consumed_offset);
   }
   g->done = reinterpret_cast<unsigned long long*>(static_cast<char*>(exchange[root]) + L.done_offset);
   g->c_root = static_cast<__half*>(c_root);
@@ -149,35 +176,47 @@ mm4_status mm4_splitk_group_create(mm4_splitk_group** out, const mm4_gemm_plan* 
   g->N = plan->d.N;
   g->splits = plan->splits;
   g->num_tiles = plan->num_tiles;
+  g->ws_bytes = plan->ws_bytes;
   *out = g;
   return MM4_OK;
 }
 
-void mm4_splitk_group_destroy(mm4_splitk_group* g) { delete g; }
+void mm4_splitk_group_destroy(mm4_splitk_group* g) {
+  if (!g) return;
+  if (g->scratch) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != g->device) cudaSetDevice(g->device);
+    cudaFree(g->scratch);
+    if (cur != g->device && cur >= 0) cudaSetDevice(cur);
+  }
+  delete g;
+}
 
 mm4_status mm4_gemm_splitk_group_run(const mm4_gemm_plan* plan, mm4_splitk_group* g, const void* A, const void* B,
-                                     const void* bias, void* workspace, size_t workspace_bytes,
-                                     mm4_stream_t stream) {
+                                     const void* bias, mm4_stream_t stream) {
   if (!plan || !g) return fail(MM4_ERR_INVALID, "null plan or group");
   if (!A || !B) return fail(MM4_ERR_INVALID, "null A/B pointer");
   if (plan->d.M != g->M || plan->d.N != g->N || plan->splits != g->splits || plan->num_tiles != g->num_tiles ||
-      (plan->pair ? 2 : 1) != g->halves)
+      (plan->pair ? 2 : 1) != g->halves || plan->ws_bytes != g->ws_bytes)
     return fail(MM4_ERR_INVALID, "plan does not match the plan the group was created for");
   if (!aligned16(A) || !aligned16(B)) return fail(MM4_ERR_INVALID, "A and B must be 16-byte aligned");
   SplitKGroupArgs ga{};
   ga.world = g->world;
   ga.rank = g->rank;
   ga.root = g->root;
+  ga.owner_mode = g->owner_mode;
   ga.num_slices = g->num_slices;
   ga.epoch = g->epoch;
-  ga.stage_rows = g->stage_rows;
+  const size_t half = static_cast<size_t>(g->epoch & 1ull) * g->half_bytes;
   for (int r = 0; r < g->world; ++r) {
-    ga.stage[r] = g->stage[r];
-    ga.flags[r] = g->flags[r];
+    ga.stage[r] = reinterpret_cast<float*>(g->exchange[r] + half);
+    ga.ready[r] = g->ready[r];
+    ga.consumed[r] = g->consumed[r];
   }
   ga.done = g->done;
   ga.c_root = g->c_root;
-  mm4_status rc = gemm_run_tc(plan, A, B, bias, g->c_root, nullptr, workspace, workspace_bytes,
+  mm4_status rc = gemm_run_tc(plan, A, B, bias, g->c_root, nullptr, g->scratch, g->ws_bytes,
                               static_cast<cudaStream_t>(stream), &ga);
   if (rc == MM4_OK) ++g->epoch;
   return rc;

@@ -151,17 +151,17 @@ class SplitKGroup:
         self._opened.append(p)
         return p
 
-    def run(self, A, B, bias=None, workspace=None, stream=None):
-        """One fused step: this rank's K shard (A [M][K_r], B [K_r][N], fp16) into the root's C."""
+    def run(self, A, B, bias=None, stream=None):
+        """One fused step: this rank's K shard (A [M][K_r], B [K_r][N], fp16) into the root's C. The
+        group owns its split-K scratch (in the exchange buffers), so no workspace is passed."""
         from .gemm import _check_tensor
         _check_tensor(A, self.plan.a_shape(), "A")
         _check_tensor(B, self.plan.b_shape(), "B")
         if self.plan.bias:
             _check_tensor(bias, (self.plan.dims.N,), "bias")
-        ws = workspace if workspace is not None else self.plan.workspace(A.device)
         self._lib.check(self._L.mm4_gemm_splitk_group_run(
             self.plan._h, self._g, A.data_ptr(), B.data_ptr(), bias.data_ptr() if self.plan.bias else None,
-            ws.data_ptr(), ws.numel(), self._lib.stream_handle(stream)))
+            self._lib.stream_handle(stream)))
         return self.C
 
     def close(self):

@@ -168,13 +168,14 @@ MM4_API mm4_status mm4_peer_close(void* ptr);
 
 /* A group of `world` ranks (<= 8) running one split-K plan, each on its own K
  * shard (same M, N, shard K, split_k on every rank), whose fp32 partials are
- * summed inside the kernels over peer memory: the CTA that finalizes a slice
- * of C on a rank stores its rows into the slice owner's exchange buffer, the
- * owner sums the ranks' rows in rank order, adds bias, rounds to fp16 and
- * writes them into the root's C. One launch per GPU and no separate
- * collective; the root's launch completes when all of C is written. Replaces
- * the NCCL reduce a multi-GPU port would put after the per-split partials of
- * matmul.swift:127-185 + the bias/cast of :21-38.
+ * summed inside the kernels over peer memory. Each rank publishes its
+ * finished fp32 slices of C into its exchange buffer; the owner of each slice
+ * (the root for groups of up to four ranks, else slice % world) reads the
+ * ranks' rows of the slice from there, sums them in rank order, adds bias,
+ * rounds to fp16 and writes the rows into the root's C. One launch per
+ * GPU and no separate collective; the root's launch completes when all of C
+ * is written. Replaces the NCCL reduce a multi-GPU port would put after the
+ * per-split partials of matmul.swift:127-185 + the bias/cast of :21-38.
  *
  * Every rank allocates an exchange buffer of mm4_splitk_group_exchange_bytes()
  * with mm4_peer_alloc; the root also allocates C [M][N] fp16 with
@@ -189,8 +190,7 @@ MM4_API mm4_status mm4_splitk_group_create(mm4_splitk_group** group, const mm4_g
                                            int32_t rank, int32_t root, void* const* exchange, void* c_root);
 MM4_API void mm4_splitk_group_destroy(mm4_splitk_group* group);
 MM4_API mm4_status mm4_gemm_splitk_group_run(const mm4_gemm_plan* plan, mm4_splitk_group* group, const void* A,
-                                             const void* B, const void* bias, void* workspace,
-                                             size_t workspace_bytes, mm4_stream_t stream);
+                                             const void* B, const void* bias, mm4_stream_t stream);
 
 /* ======================================================================== */
 /* Flash-attention forward                                                  */

@@ -54,11 +54,10 @@ def test_group_of_one_rank(cuda):
                     buildOptions=BuildOptions(splitK=16))
     grp = SplitKGroup(plan)
     try:
-        ws = plan.workspace(cuda)
         bias = _bias(cuda, N)
         for it in range(3):
             A, B = _shard(cuda, M, N, Kr, 0, it)
-            grp.run(A, B, bias, workspace=ws)
+            grp.run(A, B, bias)
             torch.cuda.synchronize()
             assert_close(grp.C.float().cpu().numpy(), _reference(cuda, M, N, Kr, 1, it).cpu().numpy(),
                          f"run {it}")
@@ -66,13 +65,14 @@ def test_group_of_one_rank(cuda):
         grp.close()
 
 
-def _worker(rank, world, port, q, M, N, Kr, split, runs):
+def _worker(rank, world, port, q, M, N, Kr, split, runs, owners):
     try:
         import datetime
 
         import torch
         import torch.distributed as dist
         os.environ["NCCL_NVLS_ENABLE"] = "0"
+        os.environ["MM4_SPLITK_GROUP_OWNERS"] = owners
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         store = dist.TCPStore("127.0.0.1", port, world_size=world + 1, is_master=False,
@@ -85,12 +85,11 @@ def _worker(rank, world, port, q, M, N, Kr, split, runs):
         plan = GemmPlan(GEMMDimensions(M, N, Kr), transpose=(False, False), bias=True,
                         buildOptions=BuildOptions(splitK=split))
         grp = SplitKGroup(plan, root=0)
-        ws = plan.workspace(dev)
         bias = _bias(dev, N)
         worst = []
         for it in range(runs):
             A, B = _shard(dev, M, N, Kr, rank, it)
-            grp.run(A, B, bias, workspace=ws)
+            grp.run(A, B, bias)
             torch.cuda.synchronize()
             if rank == 0:
                 ref = _reference(dev, M, N, Kr, world, it)
@@ -106,8 +105,11 @@ def _worker(rank, world, port, q, M, N, Kr, split, runs):
         q.put(("error", f"rank {rank}: {type(e).__name__}: {e}\n{traceback.format_exc()}"))
 
 
-@pytest.mark.parametrize("M,N,Kr,split", [(512, 512, 8192, 32), (256, 768, 4104, 8)])
-def test_two_ranks_fused_splitk(M, N, Kr, split):
+@pytest.mark.parametrize("M,N,Kr,split,owners", [(512, 512, 8192, 32, "root"), (256, 768, 4104, 8, "root"),
+                                                  (512, 512, 8192, 32, "spread")])
+def test_two_ranks_fused_splitk(M, N, Kr, split, owners):
+    """owners="root": the root finishes every slice (groups of up to four); "spread": slice % world
+    finishes it and writes the root's C over NVLink (larger groups)."""
     import datetime
 
     import torch
@@ -119,7 +121,8 @@ def test_two_ranks_fused_splitk(M, N, Kr, split):
                           timeout=datetime.timedelta(seconds=60), wait_for_workers=False)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, store.port, q, M, N, Kr, split, 4)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, store.port, q, M, N, Kr, split, 4, owners))
+             for r in range(world)]
     for p in procs:
         p.start()
     try:
