@@ -49,7 +49,7 @@ enum GemmMode : int {
 //   1. the CTA that completes the slice's rank-local sum copies the rows into
 //      its staging half for this run (two halves, by run parity), re-zeroes
 //      the scratch rows and raises ready[slice][rank] on the slice's owner
-//      (the root, or slice % world for groups of more than four);
+//      (the root, or slice % world in the spread mode);
 //   2. the owner's CTA for the slice waits for every rank's flag, reads the
 //      ranks' rows from their staging (peer loads), sums them in rank order,
 //      adds bias, rounds, stores the rows into the root's C and raises
@@ -63,7 +63,7 @@ constexpr int MM4_MAX_GROUP = 8;
 struct SplitKGroupArgs {
   int world;                     // ranks (<= 1: single GPU)
   int rank, root;
-  int owner_mode;                // 0: the root owns every slice; 1: slice % world
+  int owner_mode;                // 0: the root owns every slice; 1: slice % world (spread)
   int num_slices;                // half tiles x splits
   unsigned long long epoch;      // run index, the same on every rank
   float* stage[MM4_MAX_GROUP];   // rank r's staging half for this run [rows][ws_ld] fp32 (peer-mapped)
@@ -223,32 +223,36 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
     if (gc + 3 < args.N) b3 = __half2float(args.bias[gc + 3]);
   }
   const bool vec = (args.N & 3) == 0 && (reinterpret_cast<uintptr_t>(g.c_root) & 7u) == 0;
-  for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
-    float4 acc[4];
+  constexpr int RB = 2;  // rows per batch
+  for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += RB * RPI) {
+    // Every (source, row) load of a batch is issued before any is used: one
+    // NVLink round trip per batch, not one per source.
+    float4 v[MM4_MAX_GROUP][RB];
 #pragma unroll
     for (int src = 0; src < MM4_MAX_GROUP; ++src) {
-      if (src >= g.world) break;
-      float4 v[4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
+      for (int b = 0; b < RB; ++b) {
         const int rr = rr0 + b * RPI;
-        if (rr < r_end)
-          v[b] = __ldcg(reinterpret_cast<const float4*>(g.stage[src] + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+        if (src < g.world && rr < r_end)
+          v[src][b] = __ldcg(reinterpret_cast<const float4*>(g.stage[src] + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
       }
+    }
+    float4 acc[RB];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        if (src == 0) {
-          acc[b] = v[b];
-        } else {
-          acc[b].x += v[b].x;
-          acc[b].y += v[b].y;
-          acc[b].z += v[b].z;
-          acc[b].w += v[b].w;
+    for (int b = 0; b < RB; ++b) {
+      acc[b] = v[0][b];
+#pragma unroll
+      for (int src = 1; src < MM4_MAX_GROUP; ++src) {
+        if (src < g.world) {
+          acc[b].x += v[src][b].x;
+          acc[b].y += v[src][b].y;
+          acc[b].z += v[src][b].z;
+          acc[b].w += v[src][b].w;
         }
       }
     }
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
+    for (int b = 0; b < RB; ++b) {
       const int rr = rr0 + b * RPI;
       const int grow = row_base + rr;
       if (rr >= r_end || grow >= args.M) continue;

@@ -170,7 +170,7 @@ MM4_API mm4_status mm4_peer_close(void* ptr);
  * shard (same M, N, shard K, split_k on every rank), whose fp32 partials are
  * summed inside the kernels over peer memory. Each rank publishes its
  * finished fp32 slices of C into its exchange buffer; the owner of each slice
- * (the root for groups of up to four ranks, else slice % world) reads the
+ * (the root; slice % world with MM4_SPLITK_GROUP_OWNERS=spread) reads the
  * ranks' rows of the slice from there, sums them in rank order, adds bias,
  * rounds to fp16 and writes the rows into the root's C. One launch per
  * GPU and no separate collective; the root's launch completes when all of C
