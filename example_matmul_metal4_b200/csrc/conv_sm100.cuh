@@ -112,12 +112,20 @@ __device__ __forceinline__ ConvTileOrigin conv_tile_origin(const GemmArgs& a, co
   return o;
 }
 
-template <int BN, bool B_TMA, bool B_MN, bool A_TMA>
+// How the activations reach shared memory.
+enum : int {
+  CONV_A_GATHER = 0,  // cp.async gather warps (any stride / channel pitch)
+  CONV_A_RECT = 1,    // TMA 5-D box over a TH x TW output rectangle (stride 1)
+  CONV_A_IM2COL = 2,  // TMA im2col: 128 consecutive output pixels (stride 1)
+};
+
+template <int BN, bool B_TMA, bool B_MN, int A_MODE>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
     conv_sm100_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                       const GemmArgs args, const ConvGeom g) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr bool A_TMA = A_MODE != CONV_A_GATHER;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -179,15 +187,32 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           uint8_t* sB = ring + s * Cfg::STAGE_BYTES + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[s], A_TMA ? Cfg::STAGE_BYTES : Cfg::B_BYTES);
           if (A_TMA) {
-            // Activation box {64 ch, TW, TH, 1, 1}: the output rectangle's
-            // input footprint for this tap; padding taps read zeros (OOB fill).
-            const ConvTileOrigin o = conv_tile_origin(args, g, w.mt);
             const int kd = tap / (g.KH * g.KW);
             const int khw = tap - kd * (g.KH * g.KW);
             const int kh = khw / g.KW;
             const int kw = khw - kh * g.KW;
-            tma_load_5d(&tmX, &full[s], ring + s * Cfg::STAGE_BYTES, cb * 64, o.x + kw * g.DX, o.y + kh * g.DY,
-                        o.z + kd * g.DZ, o.n);
+            if (A_MODE == CONV_A_RECT) {
+              // Activation box {64 ch, TW, TH, 1, 1}: the output rectangle's
+              // input footprint for this tap; padding taps read zeros (OOB fill).
+              const ConvTileOrigin o = conv_tile_origin(args, g, w.mt);
+              tma_load_5d(&tmX, &full[s], ring + s * Cfg::STAGE_BYTES, cb * 64, o.x + kw * g.DX, o.y + kh * g.DY,
+                          o.z + kd * g.DZ, o.n);
+            } else {
+              // im2col: the tile is output pixels [128 mt, 128 mt + 128) in
+              // (n, oz, oy, ox) order; the load starts at the first pixel's
+              // window origin and walks the window box, this tap's offset
+              // added; padding and pixels past the end read zeros.
+              const int m0 = w.mt * GEMM_BM;
+              const int ox = m0 % g.OW;
+              const int r1 = m0 / g.OW;
+              const int oy = r1 % g.OH;
+              const int r2 = r1 / g.OH;
+              const int oz = r2 % g.OD;
+              const int n = r2 / g.OD;
+              tma_load_5d_im2col(&tmX, &full[s], ring + s * Cfg::STAGE_BYTES, cb * 64, ox - g.PL, oy - g.PT,
+                                 oz - g.PF, n, static_cast<uint16_t>(kw * g.DX), static_cast<uint16_t>(kh * g.DY),
+                                 static_cast<uint16_t>(kd * g.DZ));
+            }
           }
           if (!B_MN) {
             // [Cout][taps][Cin]: box 64(Cin) x 1(tap) x BN(Cout)

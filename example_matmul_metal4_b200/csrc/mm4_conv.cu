@@ -7,6 +7,7 @@
 // (convolution2d_padding.swift:235-290).
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 
@@ -24,7 +25,8 @@ struct mm4_conv_plan {
   bool w_tma_shape;  // weight pitch allows TMA (pointer alignment checked per run)
   bool w_mn;         // HWIO / DHWIO: Cout contiguous
   bool x_tma_shape;  // stride 1 and 16-byte channel pitch: activations by TMA
-  int tw, th;        // output rectangle per tile on the TMA path (tw * th = 128)
+  int a_mode;        // CONV_A_IM2COL or CONV_A_RECT on the TMA path
+  int tw, th;        // output rectangle per tile on the rectangle path (tw * th = 128)
   int tiles_w, tiles_h;
   char name[96];
 };
@@ -51,16 +53,31 @@ mm4_status finish_plan(mm4_conv_plan* p) {
   p->th = GEMM_BM / p->tw;
   p->tiles_w = (g.OW + p->tw - 1) / p->tw;
   p->tiles_h = (g.OH + p->th - 1) / p->th;
+  // im2col tiles are 128 consecutive output pixels: no lanes lost to a
+  // rectangle that overhangs the output width, and the fewest tiles (the
+  // last wave is the fullest). Its 5-D window box corners must fit in 5 bits
+  // signed and the tap offsets in 5 bits; the rectangle path covers the rest
+  // (MM4_CONV_ACTIVATIONS=rect forces it).
+  const int lo[3] = {-g.PL, -g.PT, -g.PF};
+  const int hi[3] = {g.OW - g.PL - g.W, g.OH - g.PT - g.H, g.OD - g.PF - g.D};
+  const int span[3] = {(g.KW - 1) * g.DX, (g.KH - 1) * g.DY, (g.KD - 1) * g.DZ};
+  bool im2col_ok = true;
+  for (int i = 0; i < 3; ++i)
+    im2col_ok = im2col_ok && lo[i] >= -16 && lo[i] <= 15 && hi[i] >= -16 && hi[i] <= 15 && span[i] <= 31;
+  const char* force = std::getenv("MM4_CONV_ACTIVATIONS");
+  if (force && std::strcmp(force, "rect") == 0) im2col_ok = false;
+  p->a_mode = im2col_ok ? CONV_A_IM2COL : CONV_A_RECT;
   snprintf(p->name, sizeof(p->name), "conv_sm100<BN=%d,%s,%s>", p->bn,
            p->w_tma_shape ? (p->w_mn ? "W:tma-MN" : "W:tma-K") : "W:gather",
-           p->x_tma_shape ? "X:tma-rect" : (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
+           p->x_tma_shape ? (p->a_mode == CONV_A_IM2COL ? "X:tma-im2col" : "X:tma-rect")
+                          : (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
   return MM4_OK;
 }
 
-template <int BN, bool B_TMA, bool B_MN, bool A_TMA>
+template <int BN, bool B_TMA, bool B_MN, int A_MODE>
 mm4_status launch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& args, const ConvGeom& g, int grid,
                   cudaStream_t st) {
-  auto kern = conv_sm100_kernel<BN, B_TMA, B_MN, A_TMA>;
+  auto kern = conv_sm100_kernel<BN, B_TMA, B_MN, A_MODE>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (rc != MM4_OK) return rc;
@@ -71,15 +88,19 @@ mm4_status launch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& 
 }
 
 template <int BN>
-mm4_status launch_bn(bool wtma, bool mn, bool xtma, const CUtensorMap& tw, const CUtensorMap& tx,
+mm4_status launch_bn(bool wtma, bool mn, int amode, const CUtensorMap& tw, const CUtensorMap& tx,
                      const GemmArgs& args, const ConvGeom& g, int grid, cudaStream_t st) {
-  if (!wtma) return launch<BN, false, false, false>(tw, tx, args, g, grid, st);
-  if (xtma) {
-    if (mn) return launch<BN, true, true, true>(tw, tx, args, g, grid, st);
-    return launch<BN, true, false, true>(tw, tx, args, g, grid, st);
+  if (!wtma) return launch<BN, false, false, CONV_A_GATHER>(tw, tx, args, g, grid, st);
+  if (amode == CONV_A_IM2COL) {
+    if (mn) return launch<BN, true, true, CONV_A_IM2COL>(tw, tx, args, g, grid, st);
+    return launch<BN, true, false, CONV_A_IM2COL>(tw, tx, args, g, grid, st);
   }
-  if (mn) return launch<BN, true, true, false>(tw, tx, args, g, grid, st);
-  return launch<BN, true, false, false>(tw, tx, args, g, grid, st);
+  if (amode == CONV_A_RECT) {
+    if (mn) return launch<BN, true, true, CONV_A_RECT>(tw, tx, args, g, grid, st);
+    return launch<BN, true, false, CONV_A_RECT>(tw, tx, args, g, grid, st);
+  }
+  if (mn) return launch<BN, true, true, CONV_A_GATHER>(tw, tx, args, g, grid, st);
+  return launch<BN, true, false, CONV_A_GATHER>(tw, tx, args, g, grid, st);
 }
 
 mm4_status check_layout_2d(int layout) {
@@ -239,16 +260,26 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
     if (rc != MM4_OK) return rc;
   }
   const bool xtma = tma && p->x_tma_shape && aligned16(x);
+  const int amode = xtma ? p->a_mode : CONV_A_GATHER;
   CUtensorMap tx;
   memset(&tx, 0, sizeof(tx));
-  if (xtma) {  // NDHWC activations: box {64 ch, TW, TH, 1, 1}
+  if (xtma) {  // NDHWC activations
     const uint64_t dims[5] = {static_cast<uint64_t>(g.C), static_cast<uint64_t>(g.W), static_cast<uint64_t>(g.H),
                               static_cast<uint64_t>(g.D), static_cast<uint64_t>(g.N)};
     const uint64_t strides[4] = {static_cast<uint64_t>(g.C) * 2, static_cast<uint64_t>(g.W) * g.C * 2,
                                  static_cast<uint64_t>(g.H) * g.W * g.C * 2,
                                  static_cast<uint64_t>(g.D) * g.H * g.W * g.C * 2};
-    const uint32_t box[5] = {64, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1, 1};
-    rc = encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (amode == CONV_A_IM2COL) {
+      // Window box of output pixel (ox, oy, oz): input origin (ox - PL, ...);
+      // the box walks origins [-PL, W - 1 + (OW - PL - W)] = OW positions.
+      const int lower[3] = {-g.PL, -g.PT, -g.PF};
+      const int upper[3] = {g.OW - g.PL - g.W, g.OH - g.PT - g.H, g.OD - g.PF - g.D};
+      rc = encode_im2col(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, lower, upper, 64, GEMM_BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {  // box {64 ch, TW, TH, 1, 1}
+      const uint32_t box[5] = {64, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1, 1};
+      rc = encode_tiled(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     if (rc != MM4_OK) return rc;
   }
 
@@ -257,7 +288,7 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   args.N = g.O;
   args.K = g.taps * g.C;
   args.num_m_tiles = p->num_m_tiles;
-  if (xtma) {
+  if (amode == CONV_A_RECT) {
     args.rowmap = 1;
     args.rm_tw = p->tw;
     args.rm_th = p->th;
@@ -280,8 +311,8 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   args.timeout_ns = wait_timeout_ns();
   const int grid = std::min(args.num_units, info.sm_count);
   for (int i = 0; i < duplicated_count; ++i) {
-    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, xtma, tm, tx, args, g, grid, st)
-                        : launch_bn<128>(tma, p->w_mn, xtma, tm, tx, args, g, grid, st);
+    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, amode, tm, tx, args, g, grid, st)
+                        : launch_bn<128>(tma, p->w_mn, amode, tm, tx, args, g, grid, st);
     if (rc != MM4_OK) return rc;
   }
   return MM4_OK;

@@ -42,6 +42,14 @@ mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t ra
                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                         CUtensorMapSwizzle swizzle);
 
+// cuTensorMapEncodeIm2col: `pixels` pixels of `channels` channels per load,
+// walking the spatial dims (innermost first, then the outermost dim) over the
+// box [lower, dim - 1 + upper] of each spatial dim (corners given in the
+// order of dims[1..rank-2]); element strides 1.
+mm4_status encode_im2col(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                         const uint64_t* dims, const uint64_t* strides_bytes, const int* lower, const int* upper,
+                         uint32_t channels, uint32_t pixels, CUtensorMapSwizzle swizzle);
+
 // Sets cudaFuncAttributeMaxDynamicSharedMemorySize once per (kernel, device).
 mm4_status ensure_smem_attr(const void* kernel, int bytes);
 

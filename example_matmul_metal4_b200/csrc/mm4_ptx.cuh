@@ -198,6 +198,18 @@ __device__ __forceinline__ void tma_load_5d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// im2col load of a 5-D NDHWC tensor: starting pixel (x = channel, w, h, d, n)
+// in input coordinates, plus the filter-tap offsets along w, h, d.
+__device__ __forceinline__ void tma_load_5d_im2col(const CUtensorMap* map, uint64_t* bar, void* dst, int c, int w,
+                                                   int h, int d, int n, uint16_t ow, uint16_t oh, uint16_t od) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5, %6, %7}], [%2], {%8, %9, %10};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(d), "r"(n), "h"(ow),
+      "h"(oh), "h"(od)
+      : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (tcgen05 / TMA) reads of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -30,6 +30,11 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode_tiled = nullptr;
+using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const int*, const int*, cuuint32_t, cuuint32_t,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeIm2colFn g_encode_im2col = nullptr;
 
 }  // namespace
 
@@ -116,6 +121,36 @@ mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t ra
   CUresult r = g_encode_tiled(map, dtype, rank, const_cast<void*>(base), d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MM4_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return MM4_OK;
+}
+
+mm4_status encode_im2col(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
+                         const uint64_t* dims, const uint64_t* strides_bytes, const int* lower, const int* upper,
+                         uint32_t channels, uint32_t pixels, CUtensorMapSwizzle swizzle) {
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!g_encode_im2col) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(MM4_ERR_CUDA, "cuTensorMapEncodeIm2col entry point unavailable");
+      g_encode_im2col = reinterpret_cast<EncodeIm2colFn>(fn);
+    }
+  }
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t es[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    es[i] = 1;
+    if (i + 1 < rank) s[i] = strides_bytes[i];
+  }
+  CUresult r = g_encode_im2col(map, dtype, rank, const_cast<void*>(base), d, s, lower, upper, channels, pixels, es,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MM4_ERR_CUDA, "cuTensorMapEncodeIm2col failed (CUresult %d)", static_cast<int>(r));
   return MM4_OK;
 }
 

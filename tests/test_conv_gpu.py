@@ -141,6 +141,33 @@ def test_conv2d_strided_dilated_aligned(cuda):
     assert_close(got, ref, "strided dilated asymmetric padding")
 
 
+@pytest.mark.parametrize("mode", ["im2col", "rect"])
+def test_stride1_activation_paths(cuda, mode, monkeypatch):
+    """Stride-1 convs with 16-byte channels load activations by TMA: im2col
+    tiles of 128 consecutive output pixels (default) or TH x TW rectangles
+    (MM4_CONV_ACTIVATIONS=rect). Dilation, asymmetric and depth padding, tiles
+    that cross rows and images, ragged last tile."""
+    if mode == "rect":
+        monkeypatch.setenv("MM4_CONV_ACTIVATIONS", "rect")
+    else:
+        monkeypatch.delenv("MM4_CONV_ACTIVATIONS", raising=False)
+    d = Conv2DDimensions(3, 19, 21, 32, 48, 3, 3, 1, 1, 2, 2, 2, 1, 0, 2)
+    x = data.normal((3, 19, 21, 32), 1.0, 7, 0)
+    w = data.normal((3, 3, 32, 48), 0.05, 7, 1)
+    b = data.uniform((48,), -0.1, 0.1, 7, 2)
+    for layout in (WEIGHTS_HWIO, WEIGHTS_OHWI):
+        plan, got, ref = _run2d(cuda, d, x, w, b, layout=layout)
+        assert f"tma-{mode}" in plan.kernel_name, plan.kernel_name
+        assert_close(got, ref, f"conv2d stride 1 {plan.kernel_name}")
+    d3 = Conv3DDimensions(2, 5, 9, 11, 16, 24, 3, 3, 3, 1, 1, 1, 1, 1, 1, 2, 0, 1, 1, 1, 0)
+    x3 = data.normal((2, 5, 9, 11, 16), 1.0, 8, 0)
+    w3 = data.normal((3, 3, 3, 16, 24), 0.03, 8, 1)
+    b3 = data.uniform((24,), -0.1, 0.1, 8, 2)
+    plan, got, ref = _run3d(cuda, d3, x3, w3, b3, layout=WEIGHTS_DHWIO)
+    assert f"tma-{mode}" in plan.kernel_name, plan.kernel_name
+    assert_close(got, ref, f"conv3d stride 1 {plan.kernel_name}")
+
+
 def test_baseline_config4_conv2d(cuda):
     """N=32, 56x56, 256->256, 3x3, pad 1, OHWI weights
     N(0,0.05), bias U[-0.1,0.1]. Oracle on a row sample; every output checked
