@@ -12,6 +12,7 @@
 #include <new>
 
 #include "conv_sm100.cuh"
+#include "conv_sm100_pair.cuh"
 #include "mm4_internal.h"
 
 using namespace mm4;
@@ -26,6 +27,7 @@ struct mm4_conv_plan {
   bool w_mn;         // HWIO / DHWIO: Cout contiguous
   bool x_tma_shape;  // stride 1 and 16-byte channel pitch: activations by TMA
   int a_mode;        // CONV_A_IM2COL or CONV_A_RECT on the TMA path
+  bool pair;         // im2col path on 2-CTA clusters (256-pixel tiles)
   int tw, th;        // output rectangle per tile on the rectangle path (tw * th = 128)
   int tiles_w, tiles_h;
   char name[96];
@@ -67,7 +69,10 @@ mm4_status finish_plan(mm4_conv_plan* p) {
   const char* force = std::getenv("MM4_CONV_ACTIVATIONS");
   if (force && std::strcmp(force, "rect") == 0) im2col_ok = false;
   p->a_mode = im2col_ok ? CONV_A_IM2COL : CONV_A_RECT;
-  snprintf(p->name, sizeof(p->name), "conv_sm100<BN=%d,%s,%s>", p->bn,
+  // CTA pairs on the im2col path (MM4_CONV_PAIR=0 keeps one-CTA tiles).
+  const char* pair_env = std::getenv("MM4_CONV_PAIR");
+  p->pair = p->x_tma_shape && p->a_mode == CONV_A_IM2COL && !(pair_env && pair_env[0] == '0');
+  snprintf(p->name, sizeof(p->name), "conv_sm100%s<BN=%d,%s,%s>", p->pair ? "_pair" : "", p->bn,
            p->w_tma_shape ? (p->w_mn ? "W:tma-MN" : "W:tma-K") : "W:gather",
            p->x_tma_shape ? (p->a_mode == CONV_A_IM2COL ? "X:tma-im2col" : "X:tma-rect")
                           : (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
@@ -84,6 +89,30 @@ mm4_status launch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& 
   kern<<<grid, CONV_THREADS, smem, st>>>(tw, tx, args, g);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "conv_sm100_kernel launch");
+  return MM4_OK;
+}
+
+template <int BN, bool B_MN>
+mm4_status launch_pair(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& args, const ConvGeom& g,
+                       int grid, cudaStream_t st) {
+  auto kern = conv_sm100_pair_kernel<BN, B_MN>;
+  constexpr int smem = ConvPairCfg<BN>::SMEM_BYTES;
+  mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
+  if (rc != MM4_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, args, g);
+  if (e != cudaSuccess) return cuda_fail(e, "conv_sm100_pair_kernel launch");
   return MM4_OK;
 }
 
@@ -248,7 +277,7 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
       const uint64_t dims[3] = {static_cast<uint64_t>(g.C), static_cast<uint64_t>(g.taps),
                                 static_cast<uint64_t>(g.O)};
       const uint64_t strides[2] = {static_cast<uint64_t>(g.C) * 2, static_cast<uint64_t>(g.taps) * g.C * 2};
-      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(p->bn)};
+      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(p->pair ? p->bn / 2 : p->bn)};
       rc = encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     } else {  // [taps][Cin][Cout]
       const uint64_t dims[3] = {static_cast<uint64_t>(g.O), static_cast<uint64_t>(g.C),
@@ -261,6 +290,7 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   }
   const bool xtma = tma && p->x_tma_shape && aligned16(x);
   const int amode = xtma ? p->a_mode : CONV_A_GATHER;
+  const bool pair = xtma && p->pair;
   CUtensorMap tx;
   memset(&tx, 0, sizeof(tx));
   if (xtma) {  // NDHWC activations
@@ -299,6 +329,7 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
     args.rm_ow = g.OW;
     args.num_m_tiles = g.N * g.OD * p->tiles_h * p->tiles_w;
   }
+  if (pair) args.num_m_tiles = static_cast<int>((p->m_total + 2 * GEMM_BM - 1) / (2 * GEMM_BM));
   args.num_n_tiles = p->num_n_tiles;
   args.num_tiles = args.num_m_tiles * p->num_n_tiles;
   args.splits = 1;
@@ -309,10 +340,17 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   args.C = static_cast<__half*>(y);
   args.status = status;
   args.timeout_ns = wait_timeout_ns();
-  const int grid = std::min(args.num_units, info.sm_count);
+  const int grid = pair ? 2 * std::min(args.num_units, info.sm_count / 2) : std::min(args.num_units, info.sm_count);
   for (int i = 0; i < duplicated_count; ++i) {
-    rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, amode, tm, tx, args, g, grid, st)
-                        : launch_bn<128>(tma, p->w_mn, amode, tm, tx, args, g, grid, st);
+    if (pair) {
+      if (p->bn == 256)
+        rc = p->w_mn ? launch_pair<256, true>(tm, tx, args, g, grid, st) : launch_pair<256, false>(tm, tx, args, g, grid, st);
+      else
+        rc = p->w_mn ? launch_pair<128, true>(tm, tx, args, g, grid, st) : launch_pair<128, false>(tm, tx, args, g, grid, st);
+    } else {
+      rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, amode, tm, tx, args, g, grid, st)
+                          : launch_bn<128>(tma, p->w_mn, amode, tm, tx, args, g, grid, st);
+    }
     if (rc != MM4_OK) return rc;
   }
   return MM4_OK;
