@@ -617,13 +617,15 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--l2", default="auto", choices=["auto", "rotate", "flush"],
                     help="keep inputs out of L2 by rotating device copies of them or by a 512 MiB write between "
-                         "steps; auto: rotate for HBM-bound workloads (a write flush leaves ~126 MB of dirty lines "
-                         "whose write-back would land inside the timed kernel), flush for tensor-bound ones")
+                         "steps; auto: rotate for HBM-bound and small workloads (a write flush leaves ~126 MB of "
+                         "dirty lines whose write-back would land inside the timed kernel), flush for the rest")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]()
     if args.l2 == "auto":
-        args.l2 = "rotate" if w.bound == "hbm" else "flush"
+        # Rotate for HBM-bound workloads and for small ones: the write flush leaves ~126 MB of dirty
+        # L2 lines whose write-back (~20 us) lands inside the next timed kernel.
+        args.l2 = "rotate" if (w.bound == "hbm" or w.bytes() < L2_BYTES / 4) else "flush"
     dist = Dist(args.gpus)
     peaks = load_peaks()
     base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,

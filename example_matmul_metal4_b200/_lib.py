@@ -97,6 +97,10 @@ SIGNATURES = {
                                                _vp]),
     "mm4_splitk_group_destroy": (None, [_vp]),
     "mm4_gemm_splitk_group_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "mm4_comm_unique_id": (ctypes.c_int, [_vp]),
+    "mm4_comm_init": (ctypes.c_int, [ctypes.POINTER(_vp), _i32, _i32, _vp]),
+    "mm4_comm_destroy": (None, [_vp]),
+    "mm4_gemm_splitk_run_distributed": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int]),
     "mm4_attention_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(AttentionDesc)]),
     "mm4_attention_plan_destroy": (None, [_vp]),
     "mm4_attention_plan_kernel_name": (ctypes.c_char_p, [_vp]),

@@ -177,6 +177,15 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   // narrow N; 128 x 512 for wide split-K).
   p->pair = p->tensor_core && d.M >= 256 && d.N >= 256;
   p->bn = (d.N <= 128) ? 128 : 256;
+  if (p->splits == 1 && p->tensor_core) {
+    // Small problems: tiles that fill the SMs matter more than the pair's
+    // lower shared-memory traffic. Use one-CTA tiles when 256 x 256 pair tiles
+    // leave most SMs idle, and 128 x 128 tiles when 128 x 256 would too.
+    const long long pair_tiles = static_cast<long long>((d.M + 255) / 256) * ((d.N + 255) / 256);
+    if (p->pair && 2 * pair_tiles < kPlanSmCount) p->pair = false;
+    const long long tiles256 = static_cast<long long>((d.M + 127) / 128) * ((d.N + 255) / 256);
+    if (!p->pair && tiles256 < kPlanSmCount) p->bn = 128;
+  }
   // Split-K with N > 256: 512-column tiles (all of TMEM, one accumulator)
   // read the fewest bytes per output, so they win when every (split, tile)
   // unit gets its own CTA (pair). When units outnumber the CTAs, CTA pairs use

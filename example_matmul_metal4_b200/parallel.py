@@ -184,3 +184,59 @@ class SplitKGroup:
         self._L.mm4_peer_free(self._own)
         if self._c_own is not None:
             self._L.mm4_peer_free(self._c_own)
+
+
+class Comm:
+    """NCCL-bootstrapped communicator for the fused multi-GPU split-K (mm4_comm_init +
+    mm4_gemm_splitk_run_distributed): the C-ABI form a caller with an NCCL unique id binds. NCCL
+    only exchanges the exchange-buffer handles at set-up; every run is one fused launch per GPU."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes):
+        import ctypes
+
+        from . import _lib
+        self._lib, self._L = _lib, _lib.lib()
+        self.nranks, self.rank = nranks, rank
+        buf = ctypes.create_string_buffer(bytes(unique_id), 128)
+        h = ctypes.c_void_p()
+        _lib.check(self._L.mm4_comm_init(ctypes.byref(h), nranks, rank, buf))
+        self._h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        import ctypes
+
+        from . import _lib
+        buf = ctypes.create_string_buffer(128)
+        _lib.check(_lib.lib().mm4_comm_unique_id(buf))
+        return buf.raw
+
+    @classmethod
+    def from_torch(cls):
+        """Collective over the default torch.distributed group: rank 0 makes the id, all ranks join."""
+        import torch.distributed as dist
+        obj = [cls.unique_id() if dist.get_rank() == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return cls(dist.get_world_size(), dist.get_rank(), obj[0])
+
+    def run(self, plan, A, B, bias=None, C=None, stream=None, duplicatedCount: int = 1):
+        """This rank's K shard of `plan` into rank 0's C (first call per plan is collective)."""
+        import torch
+
+        from .gemm import _check_tensor
+        _check_tensor(A, plan.a_shape(), "A")
+        _check_tensor(B, plan.b_shape(), "B")
+        if plan.bias:
+            _check_tensor(bias, (plan.dims.N,), "bias")
+        if self.rank == 0 and C is None:
+            C = torch.empty((plan.dims.M, plan.dims.N), dtype=torch.float16, device=A.device)
+        self._lib.check(self._L.mm4_gemm_splitk_run_distributed(
+            plan._h, self._h, A.data_ptr(), B.data_ptr(), bias.data_ptr() if plan.bias else None,
+            C.data_ptr() if C is not None else None, self._lib.stream_handle(stream), int(duplicatedCount)))
+        return C
+
+    def close(self):
+        """Collective: releases the communicator and every plan's group."""
+        if self._h is not None:
+            self._L.mm4_comm_destroy(self._h)
+            self._h = None

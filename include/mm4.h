@@ -192,6 +192,23 @@ MM4_API void mm4_splitk_group_destroy(mm4_splitk_group* group);
 MM4_API mm4_status mm4_gemm_splitk_group_run(const mm4_gemm_plan* plan, mm4_splitk_group* group, const void* A,
                                              const void* B, const void* bias, mm4_stream_t stream);
 
+/* Communicator form of the same fused multi-GPU split-K, bootstrapped from an
+ * NCCL unique id (rank 0 calls mm4_comm_unique_id and hands the 128 bytes to
+ * every rank, e.g. over MPI or a launcher store). mm4_comm_init creates the
+ * NCCL communicator (libnccl.so.2 is loaded at run time); the first
+ * mm4_gemm_splitk_run_distributed call for a plan is collective and sets up
+ * the plan's split-K group over it (exchange buffers, IPC handle exchange);
+ * later calls are one fused launch per GPU. Every rank passes its own K shard
+ * (A [M][K_r], B [K_r][N]) and the same bias; rank 0 receives C [M][N] fp16
+ * (other ranks may pass C = NULL). mm4_comm_destroy is collective. */
+typedef struct mm4_comm mm4_comm;
+MM4_API mm4_status mm4_comm_unique_id(void* nccl_unique_id /* 128 bytes */);
+MM4_API mm4_status mm4_comm_init(mm4_comm** comm, int32_t nranks, int32_t rank, const void* nccl_unique_id);
+MM4_API void mm4_comm_destroy(mm4_comm* comm);
+MM4_API mm4_status mm4_gemm_splitk_run_distributed(const mm4_gemm_plan* plan, mm4_comm* comm, const void* A,
+                                                   const void* B, const void* bias, void* C, mm4_stream_t stream,
+                                                   int duplicated_count);
+
 /* ======================================================================== */
 /* Flash-attention forward                                                  */
 /* ======================================================================== */

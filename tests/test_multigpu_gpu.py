@@ -134,3 +134,70 @@ def test_two_ranks_fused_splitk(M, N, Kr, split, owners):
                 p.kill()
     assert kind == "ok", payload
     assert max(payload) <= 0.0, payload
+
+
+def _comm_worker(rank, world, port, q, M, N, Kr, split, runs):
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        store = dist.TCPStore("127.0.0.1", port, world_size=world + 1, is_master=False,
+                              timeout=datetime.timedelta(seconds=60))
+        sys.path.insert(0, str(ROOT))
+        from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan
+        from example_matmul_metal4_b200.parallel import Comm
+        # NCCL bootstrap the C-ABI way: rank 0 makes the unique id, the store carries it.
+        if rank == 0:
+            store.set("mm4_nccl_id", Comm.unique_id())
+        uid = store.get("mm4_nccl_id")
+        comm = Comm(world, rank, uid)
+        plan = GemmPlan(GEMMDimensions(M, N, Kr), transpose=(False, False), bias=True,
+                        buildOptions=BuildOptions(splitK=split))
+        bias = _bias(dev, N)
+        C = torch.empty((M, N), dtype=torch.float16, device=dev) if rank == 0 else None
+        worst = []
+        for it in range(runs):
+            A, B = _shard(dev, M, N, Kr, rank, it)
+            comm.run(plan, A, B, bias, C=C)
+            torch.cuda.synchronize()
+            if rank == 0:
+                ref = _reference(dev, M, N, Kr, world, it)
+                worst.append(((C.float() - ref).abs() - (2e-2 + 1e-2 * ref.abs())).max().item())
+        comm.close()
+        if rank == 0:
+            q.put(("ok", worst))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put(("error", f"rank {rank}: {type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+def test_two_ranks_nccl_bootstrapped_comm():
+    """mm4_comm_init from an NCCL unique id + mm4_gemm_splitk_run_distributed (the same fused kernel)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    store = dist.TCPStore("127.0.0.1", 0, world_size=world + 1, is_master=True,
+                          timeout=datetime.timedelta(seconds=60), wait_for_workers=False)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_comm_worker, args=(r, world, store.port, q, 512, 512, 8192, 32, 3))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        kind, payload = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert kind == "ok", payload
+    assert max(payload) <= 0.0, payload
