@@ -661,6 +661,9 @@ def main():
         cpu = None
         if args.gpus == 1 and not args.no_cpu_baseline:
             cpu = cpu_sample(w, seconds_hint=args.cpu_seconds)
+            # The reference's own CPU check runs single-threaded; time that too on a smaller sample.
+            one = cpu_sample(w, seconds_hint=max(1.0, args.cpu_seconds / 4), threads=1)
+            cpu["single_thread"] = {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}
         cfg["kernel"] = res["kernel"]
         cfg["l2"] = cfg["l2"].replace("{n}", str(res["nsets"]))
         if args.gpus == 1:
