@@ -104,3 +104,46 @@ def test_no_device_means_not_supported():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     assert _lib.lib().mm4_device_supported() == 0
+
+
+def test_splitk_group_sizing_and_validation():
+    """Host-side checks of the multi-GPU split-K group entry points (no device work)."""
+    lib = _lib.lib()
+    rc, plan = _gemm(M=512, N=512, K=65536, split_k=32)
+    assert rc == 0
+    nbytes = ctypes.c_size_t()
+    # staging: 2 halves x [512 rows][512] fp32; flags: ready 128 slices x world, consumed + done 128 each
+    for world in (1, 2, 8):
+        assert lib.mm4_splitk_group_exchange_bytes(plan, world, ctypes.byref(nbytes)) == 0
+        slices = 2 * 2 * 32  # 2 pair tiles x 2 row halves x 32 splits
+        assert nbytes.value == 2 * 512 * 512 * 4 + slices * world * 8 + 2 * slices * 8
+    assert lib.mm4_splitk_group_exchange_bytes(plan, 9, ctypes.byref(nbytes)) == _lib.MM4_ERR_UNSUPPORTED
+    assert lib.mm4_splitk_group_exchange_bytes(plan, 0, ctypes.byref(nbytes)) == _lib.MM4_ERR_UNSUPPORTED
+    g = ctypes.c_void_p()
+    ptrs = (ctypes.c_void_p * 2)(0x100000, 0x200000)
+    assert lib.mm4_splitk_group_create(ctypes.byref(g), plan, 2, 2, 0, ptrs, ctypes.c_void_p(0x300000)) == \
+        _lib.MM4_ERR_INVALID  # rank out of range
+    bad = (ctypes.c_void_p * 2)(0x100000, 0x200010)
+    assert lib.mm4_splitk_group_create(ctypes.byref(g), plan, 2, 0, 0, bad, ctypes.c_void_p(0x300000)) == \
+        _lib.MM4_ERR_INVALID  # exchange buffers must be 256-byte aligned
+    assert b"256-byte" in lib.mm4_last_error()
+    lib.mm4_gemm_plan_destroy(plan)
+    rc, direct = _gemm(M=512, N=512, K=4096, split_k=1)
+    assert lib.mm4_splitk_group_exchange_bytes(direct, 2, ctypes.byref(nbytes)) == _lib.MM4_ERR_UNSUPPORTED
+    lib.mm4_gemm_plan_destroy(direct)
+
+
+def test_comm_and_peer_argument_checks():
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(128)
+    assert lib.mm4_comm_init(ctypes.byref(h), 0, 0, uid) == _lib.MM4_ERR_INVALID
+    assert lib.mm4_comm_init(ctypes.byref(h), 9, 0, uid) == _lib.MM4_ERR_INVALID
+    assert lib.mm4_comm_init(ctypes.byref(h), 2, 2, uid) == _lib.MM4_ERR_INVALID
+    assert lib.mm4_comm_init(ctypes.byref(h), 2, 0, None) == _lib.MM4_ERR_INVALID
+    p = ctypes.c_void_p()
+    assert lib.mm4_peer_alloc(0, ctypes.byref(p), ctypes.byref(_lib.PeerHandle())) == _lib.MM4_ERR_INVALID
+    assert lib.mm4_peer_free(None) == 0 and lib.mm4_peer_close(None) == 0
+    rc, plan = _gemm(M=512, N=512, K=65536, split_k=32)
+    assert lib.mm4_gemm_splitk_run_distributed(plan, None, None, None, None, None, None, 1) == _lib.MM4_ERR_INVALID
+    lib.mm4_gemm_plan_destroy(plan)
