@@ -164,17 +164,13 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   const bool a_ok = d.transpose_left ? (d.M % 8 == 0) : (d.K % 8 == 0);
   const bool b_ok = d.transpose_right ? (d.K % 8 == 0) : (d.N % 8 == 0);
   p->tensor_core = a_ok && b_ok;
-  // Split-K runs few, K-heavy units: a 128 x 512 tile (one TMEM-wide
-  // accumulator) reads each A k-slab once per 512 columns. Otherwise 128 x 256
-  // with a double-buffered accumulator, or 128 x 128 for narrow N.
   p->kb_total = (d.K + GEMM_BK - 1) / GEMM_BK;
   p->splits = std::max(1, std::min(d.split_k, p->kb_total));
   if (!p->tensor_core) p->splits = 1;
   // Tile choice. CTA pairs (cta_group::2, 256-row tiles, each CTA staging half
-  // of B) when M and N are both at least 256; split-K then uses 256 x 512 pair
-  // tiles (one TMEM-wide accumulator per CTA) so each A k-slab is read once
-  // per 512 columns. Otherwise one CTA with 128 x 256 (or 128 x 128 for
-  // narrow N; 128 x 512 for wide split-K).
+  // of B) when M and N are both at least 256, otherwise one CTA with 128 x 256
+  // (128 x 128 for narrow N); the adjustments below cover small problems and
+  // split-K.
   p->pair = p->tensor_core && d.M >= 256 && d.N >= 256;
   p->bn = (d.N <= 128) ? 128 : 256;
   if (p->splits == 1 && p->tensor_core) {
