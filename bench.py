@@ -198,6 +198,9 @@ class Dist:
         import datetime
         import torch.distributed as dist
         if self.world > 1:
+            # The bench's collectives are a few bytes (barriers, timing max, set-up handles): NVLink
+            # multicast (NVLS) buys nothing here, so keep NCCL on plain peer transport.
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
             dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=60))
             self.pg = dist
 
