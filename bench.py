@@ -602,7 +602,7 @@ def cpu_sample(w, seconds_hint=10.0, threads=None):
         sample = (f"{rows} output rows ({w.W} pixels x {w.O} channels each) of one image of the {w.name} conv "
                   f"(ConvolutionShared.swift:4994-5096), {dt:.2f} s")
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": sample + ", extrapolated linearly to the full workload"}
+            "sample": sample + "; the sample's rate stands for the full workload"}
 
 
 # ---------------------------------------------------------------------------
