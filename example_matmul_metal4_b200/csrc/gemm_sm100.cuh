@@ -186,32 +186,37 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
   const int tr = ethread / TPR;
   const int gc = col0 + (ethread % TPR) * 4;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  // 1. Publish (the staging half is free: group_unit_start checked it):
-  //    rows scratch -> staging, scratch re-zeroed, flag on the owner.
+  // 1. A rank that does not own the slice publishes it (the staging half is
+  //    free: group_unit_start checked it): rows scratch -> staging, scratch
+  //    re-zeroed, flag on the owner. The owner reads its own rows straight
+  //    from its scratch in step 2.
   float* stage = g.stage[g.rank];
-  for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
-    float4 v[4];
+  if (owner != g.rank) {
+    for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
+      float4 v[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int rr = rr0 + b * RPI;
-      if (rr < r_end) v[b] = __ldcg(reinterpret_cast<const float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
-    }
+      for (int b = 0; b < 4; ++b) {
+        const int rr = rr0 + b * RPI;
+        if (rr < r_end) v[b] = __ldcg(reinterpret_cast<const float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+      }
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int rr = rr0 + b * RPI;
-      if (rr >= r_end) break;
-      const size_t off = static_cast<size_t>(row_base + rr) * args.ws_ld + gc;
-      __stcg(reinterpret_cast<float4*>(args.ws + off), zero);
-      __stcg(reinterpret_cast<float4*>(stage + off), v[b]);
+      for (int b = 0; b < 4; ++b) {
+        const int rr = rr0 + b * RPI;
+        if (rr >= r_end) break;
+        const size_t off = static_cast<size_t>(row_base + rr) * args.ws_ld + gc;
+        __stcg(reinterpret_cast<float4*>(args.ws + off), zero);
+        __stcg(reinterpret_cast<float4*>(stage + off), v[b]);
+      }
     }
+    named_barrier(1, 128);  // orders every thread's stores before the release
+    if (ethread == 0) st_release_sys_u64(g.ready[owner] + static_cast<size_t>(slice) * g.world + g.rank, tag);
+    return;
   }
-  named_barrier(1, 128);  // orders every thread's stores before the release
-  if (ethread == 0) st_release_sys_u64(g.ready[owner] + static_cast<size_t>(slice) * g.world + g.rank, tag);
-  if (owner != g.rank) return;
-  // 2. Owner: one thread per rank polls that rank's flag; then every rank's
-  //    rows (peer loads, up to four rows per source in flight), summed in
-  //    rank order, bias, fp16 into the root's C.
-  const bool ok = ethread >= g.world ||
+  // 2. Owner: one thread per other rank polls that rank's flag; then every
+  //    rank's rows (peer loads, this rank's own from its scratch; all loads
+  //    of a row batch in flight at once), summed in rank order, bias, fp16
+  //    into the root's C; this rank's scratch rows re-zeroed.
+  const bool ok = ethread >= g.world || ethread == g.rank ||
                   wait_all_ge_sys_u64(g.ready[g.rank] + static_cast<size_t>(slice) * g.world + ethread, 1, tag, wd,
                                       SITE_GEMM_GROUP_FLAGS);
   if (!named_barrier_and(1, 128, ok)) return;
@@ -233,9 +238,16 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
 #pragma unroll
       for (int b = 0; b < RB; ++b) {
         const int rr = rr0 + b * RPI;
-        if (src < g.world && rr < r_end)
-          v[src][b] = __ldcg(reinterpret_cast<const float4*>(g.stage[src] + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+        if (src < g.world && rr < r_end) {
+          const float* from = src == g.rank ? args.ws : g.stage[src];
+          v[src][b] = __ldcg(reinterpret_cast<const float4*>(from + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+        }
       }
+    }
+#pragma unroll
+    for (int b = 0; b < RB; ++b) {
+      const int rr = rr0 + b * RPI;
+      if (rr < r_end) __stcg(reinterpret_cast<float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc), zero);
     }
     float4 acc[RB];
 #pragma unroll
