@@ -46,15 +46,17 @@ enum GemmMode : int {
 // rank publishes finished slices (a 128-row half tile x one split's row
 // range) into a staging area of its exchange buffer, which every other rank
 // maps. Per slice:
-//   1. the CTA that completes the slice's rank-local sum copies the rows into
-//      its staging half for this run (two halves, by run parity), re-zeroes
-//      the scratch rows and raises ready[slice][rank] on the slice's owner
-//      (the root, or slice % world in the spread mode);
-//   2. the owner's CTA for the slice waits for every rank's flag, reads the
-//      ranks' rows from their staging (peer loads), sums them in rank order,
-//      adds bias, rounds, stores the rows into the root's C and raises
-//      consumed[slice] on every rank (and done[slice] on the root when it is
-//      not the root itself);
+//   1. on a rank that does not own the slice (the owner is the root, or
+//      slice % world in the spread mode), the CTA that completes the slice's
+//      rank-local sum copies the rows into its staging half for this run (two
+//      halves, by run parity), re-zeroes the scratch rows and raises
+//      ready[slice][rank] on the owner;
+//   2. the owner's CTA for the slice waits for the other ranks' flags, reads
+//      their rows from their staging (peer loads) and its own from its
+//      scratch, sums them in rank order, adds bias, rounds, stores the rows
+//      into the root's C (and raises done[slice] on the root when it is not
+//      the root itself); at its next launch it raises consumed[slice] on
+//      every rank;
 //   3. a rank overwrites a staging half (two runs later) only after the owner
 //      consumed it; the root's launch ends once every slice is in C.
 // Cross-GPU traffic is peer loads (and C stores) plus release/acquire flags
