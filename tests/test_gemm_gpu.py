@@ -50,6 +50,31 @@ def test_baseline_config1_1024_nn_bias(cuda):
     assert_close(got, ref, "1024^3")
 
 
+def test_8192_cube_vs_fp32_reference(cuda):
+    """The north-star 8192^3 GEMM+bias at full size (CTA-pair kernel): every output against a plain
+    PyTorch fp32 GEMM (TF32 off) of the same fp16 inputs, plus the C oracle on a row sample."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    M = N = K = 8192
+    g = torch.Generator(device=cuda)
+    g.manual_seed(11)
+    A = (torch.rand((M, K), generator=g, device=cuda) * 2 - 1).half()
+    B = (torch.rand((K, N), generator=g, device=cuda) * 2 - 1).half()
+    b = (torch.rand((N,), generator=g, device=cuda) * 2 - 1).half()
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True)
+    assert "pair" in plan.kernel_name
+    C = plan.run(A, B, b)
+    sync_check()
+    ref = torch.addmm(b.float(), A.float(), B.float())
+    err = (C.float() - ref).abs()
+    bad = int((err > 2e-2 + 1e-2 * ref.abs()).sum().item())
+    assert bad == 0, f"{bad} mismatches, max abs err {err.max().item():.4g}"
+    rows = (4096, 4100)
+    ref_rows = oracle.gemm(A.cpu().numpy(), B.cpu().numpy(), b.cpu().numpy(), M, N, K, rows=rows,
+                           threads=oracle.default_threads())
+    assert_close(C[rows[0]:rows[1]].float().cpu().numpy(), ref_rows, "8192^3 oracle rows")
+
+
 @pytest.mark.parametrize("M,N,K", [(200, 136, 200), (129, 264, 72), (1, 8, 8), (130, 520, 1000), (64, 64, 64)])
 def test_edges_and_k_tails(cuda, M, N, K):
     plan, got, ref = _run(cuda, M, N, K, False, False)
