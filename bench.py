@@ -413,6 +413,13 @@ def build_gemm(w, dist, dev, gen, l2):
         t = nxt()
         plan.run(t["A"], t["B"], bias, C=C, workspace=ws)
 
+    Ct = torch.empty_like(C)
+
+    def torch_step():
+        t = nxt()
+        torch.addmm(bias, t["A"], t["B"], out=Ct)
+    step.comparator = ("torch.addmm (cuBLAS, fp16 in/out)", torch_step, lambda: C, lambda: Ct)
+
     hA, hB, hb = A.cpu().pin_memory(), B.cpu().pin_memory(), bias.cpu().pin_memory()
     hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
 
@@ -439,6 +446,13 @@ def build_attention(w, dist, dev, gen, l2):
     def step():
         t = nxt()
         plan.run(t["Q"], t["K"], t["V"], O=O)
+
+    Ot = [None]
+
+    def torch_step():
+        t = nxt()
+        Ot[0] = torch.nn.functional.scaled_dot_product_attention(t["Q"], t["K"], t["V"])
+    step.comparator = ("torch scaled_dot_product_attention (fp16)", torch_step, lambda: O, lambda: Ot[0])
 
     hQ, hK, hV = Q.cpu().pin_memory(), K.cpu().pin_memory(), V.cpu().pin_memory()
     hO = torch.empty(O.shape, dtype=O.dtype).pin_memory()
@@ -471,6 +485,18 @@ def build_conv(w, dist, dev, gen, l2):
     def step():
         t = nxt()
         plan.run(t["x"], t["w"], bias, y=y)
+
+    yt = [None]
+    F = torch.nn.functional
+    # NHWC / NDHWC tensors as channels-last views of the NCHW / NCDHW shapes cuDNN takes.
+    perm_x = (0, 4, 1, 2, 3) if w.three_d else (0, 3, 1, 2)
+    perm_y = (0, 2, 3, 4, 1) if w.three_d else (0, 2, 3, 1)
+    conv = F.conv3d if w.three_d else F.conv2d
+
+    def torch_step():
+        t = nxt()
+        yt[0] = conv(t["x"].permute(*perm_x), t["w"].permute(*perm_x), bias, padding=1).permute(*perm_y)
+    step.comparator = (f"torch {conv.__name__} (cuDNN, fp16, channels-last)", torch_step, lambda: y, lambda: yt[0])
 
     hx, hw, hb = x.cpu().pin_memory(), wt.cpu().pin_memory(), bias.cpu().pin_memory()
     hy = torch.empty(plan.out_shape, dtype=torch.float16).pin_memory()
@@ -521,6 +547,21 @@ def run_mm4(args, w, dist, peaks):
         e2e_ms = dist.max(sum(time_steps(e2e_step, n_e2e, 2, flush, stream, dist)) / n_e2e)
         e2e = {"value": units * w.flops() / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(e2e_bytes[0]), "d2h_bytes_per_step": int(e2e_bytes[1])}
+    comparator = None
+    if dist.world == 1 and hasattr(step, "comparator") and not args.no_comparator:
+        # B200 analogue of the reference's MPSGraph agreement check: the same op through torch
+        # (cuBLAS / SDPA / cuDNN) on the same inputs, timed the same way, outputs compared.
+        name, torch_step, ours, theirs = step.comparator
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False  # fp32 accumulation
+        cmp_ms = sum(time_steps(torch_step, args.steps, args.warmup, flush, stream, dist)) / args.steps
+        step()
+        torch_step()  # every input copy holds the same values, so both outputs are comparable
+        torch.cuda.synchronize()
+        a, b = ours().float(), theirs().float()
+        diff = (a - b).abs()
+        comparator = {"impl": name, "ms_per_step": cmp_ms, "value": w.flops() / (cmp_ms * 1e-3) / 1e12,
+                      "unit": "TFLOP/s", "max_abs_diff_vs_mm4": float(diff.max().item()),
+                      "mismatches_vs_mm4": int((diff > 2e-2 + 1e-2 * b.abs()).sum().item())}
     if hasattr(step, "close"):
         step.close()  # collective on every rank (peer mappings, exchange buffers)
 
@@ -536,7 +577,7 @@ def run_mm4(args, w, dist, peaks):
                 "algorithmic_bytes": w.bytes(), "algorithmic_flops": w.flops(),
                 "traffic": load_traffic(w.name), "kernel": kernel_name, "kernel_ms": ms}
     return dict(value=value, ms=ms, clocks=clk, e2e=e2e, roofline=roof, launches=launches * args.steps,
-                kernel=kernel_name, scaling=scaling, nsets=nsets)
+                kernel=kernel_name, scaling=scaling, nsets=nsets, comparator=comparator)
 
 
 # ---------------------------------------------------------------------------
@@ -617,6 +658,7 @@ def main():
     ap.add_argument("--workload", default="splitk", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="mm4", choices=["mm4", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-comparator", action="store_true", help="skip the torch (cuBLAS/SDPA/cuDNN) comparator")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--l2", default="auto", choices=["auto", "rotate", "flush"],
                     help="keep inputs out of L2 by rotating device copies of them or by a 512 MiB write between "
@@ -680,7 +722,7 @@ def main():
         line = dict(base, value=res["value"], ms_per_step=res["ms"], scaling=res["scaling"], config=cfg,
                     pct_of_measured_bf16_peak=res["value"] / args.gpus / peaks["bf16_tflops"],
                     clocks=res["clocks"], e2e=res["e2e"], roofline=res["roofline"], cpu_baseline=cpu,
-                    gpu_launches=res["launches"])
+                    gpu_launches=res["launches"], comparator=res["comparator"])
         print(json.dumps(line), flush=True)
     dist.close()
 

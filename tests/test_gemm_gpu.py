@@ -50,6 +50,14 @@ def test_baseline_config1_1024_nn_bias(cuda):
     assert_close(got, ref, "1024^3")
 
 
+def test_reference_nt_shape_split30(cuda):
+    """The reference's own NT split-K run (matmul.swift:335): M=32, N=3072, K=80000, B stored [N][K],
+    splitK 30 -- more (split, tile) units than CTAs, so the last-arriving split finalizes each tile."""
+    plan, got, ref = _run(cuda, 32, 3072, 80000, False, True, split=30, seed=5)
+    assert "splitk" in plan.kernel_name
+    assert_close(got, ref, "32x3072x80000 NT split 30")
+
+
 def test_8192_cube_vs_fp32_reference(cuda):
     """The north-star 8192^3 GEMM+bias at full size (CTA-pair kernel): every output against a plain
     PyTorch fp32 GEMM (TF32 off) of the same fp16 inputs, plus the C oracle on a row sample."""
