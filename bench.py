@@ -553,7 +553,14 @@ def run_mm4(args, w, dist, peaks):
         # (cuBLAS / SDPA / cuDNN) on the same inputs, timed the same way, outputs compared.
         name, torch_step, ours, theirs = step.comparator
         torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False  # fp32 accumulation
+        # Same thermal state as the mm4 arm: the same untimed burn before and after the timed steps, and
+        # its own clock record (a long dense run settles at power-capped clocks; a cold one boosts).
+        cmp_clocks = ClockSampler(dist.local_rank)
+        cmp_clocks.start()
+        burn(torch_step, flush, 0.6, dist)
         cmp_ms = sum(time_steps(torch_step, args.steps, args.warmup, flush, stream, dist)) / args.steps
+        burn(torch_step, flush, 0.3, dist)
+        cmp_clk = cmp_clocks.stop()
         step()
         torch_step()  # every input copy holds the same values, so both outputs are comparable
         torch.cuda.synchronize()
@@ -561,7 +568,8 @@ def run_mm4(args, w, dist, peaks):
         diff = (a - b).abs()
         comparator = {"impl": name, "ms_per_step": cmp_ms, "value": w.flops() / (cmp_ms * 1e-3) / 1e12,
                       "unit": "TFLOP/s", "max_abs_diff_vs_mm4": float(diff.max().item()),
-                      "mismatches_vs_mm4": int((diff > 2e-2 + 1e-2 * b.abs()).sum().item())}
+                      "mismatches_vs_mm4": int((diff > 2e-2 + 1e-2 * b.abs()).sum().item()),
+                      "clocks": cmp_clk}
     if hasattr(step, "close"):
         step.close()  # collective on every rank (peer mappings, exchange buffers)
 

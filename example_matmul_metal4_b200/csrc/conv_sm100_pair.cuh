@@ -7,6 +7,16 @@
 // third against the one-CTA kernel; with BN = 128 (Cout = 128) the one-CTA
 // kernel's N = 128 instructions are bound by shared-memory reads.
 //
+// Tap rows (TAPROW): for dilation-1 filters 2 or 3 taps wide, the tile walks
+// virtual pixels of rows OW + KW - 1 wide, and one im2col box of
+// 128 + KW - 1 pixels per (kd, kh, channel slab) feeds all KW taps: tap kw
+// is the same box read from row kw on, so its MMA descriptors start kw
+// 128-byte rows further. TMA writes the 128-byte swizzle by absolute
+// shared-memory address and tcgen05 reads it the same way, so a start that
+// is a whole number of rows into a 1024-byte-aligned box reads those rows
+// unchanged. Activation bytes per MMA flop drop by a factor of KW; the KW - 1
+// virtual columns per row are computed and not stored (3 % at W = 64).
+//
 // Roles as in the CTA-pair GEMM (gemm_sm100_pair.cuh): warp 0 of both CTAs
 // issues TMA into its own ring with completion counted on the leader's full
 // barrier, the leader's warp 1 issues the MMAs and commits to both CTAs,
@@ -18,14 +28,23 @@
 
 namespace mm4 {
 
-template <int BN>
+// TAPROW: a stage holds one activation box of up to 130 pixels (136 rows
+// reserved, a whole number of 1024-byte swizzle atoms) and the weights of up
+// to CONV_ROW_MAX_KW taps.
+constexpr int CONV_ROW_MAX_KW = 3;
+
+template <int BN, bool TAPROW = false>
 struct ConvPairCfg {
-  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;   // 16 KB: this CTA's 128 pixels x 64 channels
-  static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;  // this CTA's half of the weight columns
+  static constexpr int A_ROWS = TAPROW ? GEMM_BM + 8 : GEMM_BM;
+  static constexpr int A_BYTES = A_ROWS * GEMM_BK * 2;     // this CTA's pixels x 64 channels
+  static constexpr int B_TAP_BYTES = (BN / 2) * GEMM_BK * 2;  // this CTA's half of one tap's weight columns
+  static constexpr int B_BYTES = (TAPROW ? CONV_ROW_MAX_KW : 1) * B_TAP_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 128) ? 8 : 6;
+  static constexpr int STAGES = TAPROW ? ((BN == 128) ? 5 : 3) : ((BN == 128) ? 8 : 6);
   static constexpr int TMEM_COLS = 2 * BN;                 // two accumulators
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+  static_assert(A_BYTES % 1024 == 0 && STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte swizzle alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 };
 
 enum : int {
@@ -36,11 +55,11 @@ enum : int {
   SITE_CONVPAIR_MMA_DRAIN = 74,
 };
 
-template <int BN, bool B_MN>
+template <int BN, bool B_MN, bool TAPROW>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     conv_sm100_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                            const GemmArgs args, const ConvGeom g) {
-  using Cfg = ConvPairCfg<BN>;
+  using Cfg = ConvPairCfg<BN, TAPROW>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_f16_f32(2 * GEMM_BM, BN, false, B_MN);
   constexpr int HALF_N = BN / 2;
@@ -96,10 +115,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int u = u0; u < args.num_units && ok; u += ustep) {
         const GemmUnit w = gemm_decode_unit(args, u);
-        // This CTA's 128 output pixels start at m0 (n, oz, oy, ox order).
+        // This CTA's 128 output pixels start at m0 (n, oz, oy, ox order; ox
+        // runs over the virtual row width with TAPROW).
         const int m0 = w.mt * 2 * GEMM_BM + static_cast<int>(rank) * GEMM_BM;
-        const int ox = m0 % g.OW;
-        const int r1 = m0 / g.OW;
+        const int row_w = TAPROW ? args.rm_vw : g.OW;
+        const int ox = m0 % row_w;
+        const int r1 = m0 / row_w;
         const int oy = r1 % g.OH;
         const int r2 = r1 / g.OH;
         const int oz = r2 % g.OD;
@@ -115,6 +136,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* sA = ring + s * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
           const uint32_t lbar = mapa_shared(smem_u32(&full[s]), 0);
+          if constexpr (TAPROW) {
+            // k-block kb = (kd, kh, slab): one box of 128 + KW - 1 pixels and
+            // the weights of taps (kd, kh, 0 .. KW-1).
+            if (rank == 0)
+              mbar_arrive_expect_tx(&full[s], 2u * ((GEMM_BM + g.KW - 1) * GEMM_BK * 2 + g.KW * Cfg::B_TAP_BYTES));
+            const int khd = kb / g.ncb;
+            const int cb = kb - khd * g.ncb;
+            const int kd = khd / g.KH;
+            const int kh = khd - kd * g.KH;
+            tma_load_5d_im2col_pair(&tmX, lbar, sA, cb * 64, ox - g.PL, oy - g.PT, oz - g.PF, n, 0,
+                                    static_cast<uint16_t>(kh * g.DY), static_cast<uint16_t>(kd * g.DZ));
+            for (int kw = 0; kw < g.KW; ++kw) {
+              const int tap = khd * g.KW + kw;
+              uint8_t* sBt = sB + kw * Cfg::B_TAP_BYTES;
+              if (!B_MN) {
+                tma_load_3d_pair(&tmW, lbar, sBt, cb * 64, tap, n0);
+              } else {
+#pragma unroll
+                for (int j = 0; j < HALF_N / 64; ++j)
+                  tma_load_3d_pair(&tmW, lbar, sBt + j * 8192, n0 + 64 * j, cb * 64, tap);
+              }
+            }
+            ++fills;
+            continue;
+          }
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
           const int tap = kb / g.ncb;
           const int cb = kb - tap * g.ncb;
@@ -166,11 +212,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tc_fence_after();
           const uint32_t a_base = smem_u32(ring + s * Cfg::STAGE_BYTES);
           const uint32_t b_base = a_base + Cfg::A_BYTES;
+          const int taps_here = TAPROW ? g.KW : 1;
+          for (int kw = 0; kw < taps_here; ++kw) {
+            // TAPROW: tap kw reads the box from pixel row kw on.
+            const uint32_t a_tap = a_base + static_cast<uint32_t>(kw) * 128u;
+            const uint32_t b_tap = b_base + static_cast<uint32_t>(kw) * Cfg::B_TAP_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-            const uint64_t adesc = sw128_desc(a_base + kk * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? sw128_desc(b_base + kk * 2048, 8192, 1024) : sw128_desc(b_base + kk * 32, 16, 1024);
-            umma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+              const uint64_t adesc = sw128_desc(a_tap + kk * 32, 16, 1024);
+              const uint64_t bdesc =
+                  B_MN ? sw128_desc(b_tap + kk * 2048, 8192, 1024) : sw128_desc(b_tap + kk * 32, 16, 1024);
+              umma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb > w.kb0 || kw > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit_pair(&empty[s], 0x3);
           ++consumed;

@@ -94,8 +94,13 @@ struct GemmArgs {
   // Output row map of the direct epilogue. 0: tile row r is output row
   // mt*128 + r (GEMM). 1: a tile is a rm_th x rm_tw rectangle of output
   // pixels of one (n, oz) plane (convolution with TMA-fed activations).
+  // 2: tile rows are virtual pixels of rows rm_vw wide (output width plus
+  // the filter's kw overhang); virtual pixel v is output pixel
+  // (v / rm_vw) * rm_ow + v % rm_vw when v % rm_vw < rm_ow and
+  // v / rm_vw < rm_vrows, otherwise it is not stored.
   int rowmap;
   int rm_tw, rm_th, rm_tiles_w, rm_tiles_h, rm_od, rm_oh, rm_ow;
+  int rm_vw, rm_vrows;
   int* status;
   unsigned long long timeout_ns;
   SplitKGroupArgs grp;    // multi-GPU split-K (grp.world > 1), cooperative finalize only
@@ -431,6 +436,11 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
       const int ow = twi * args.rm_tw + row_in_tile % args.rm_tw;
       row_ok = oh < args.rm_oh && ow < args.rm_ow;
       row = ((n * args.rm_od + oz) * args.rm_oh + oh) * args.rm_ow + ow;
+    } else if (args.rowmap == 2) {
+      const int xv = row % args.rm_vw;
+      const int line = row / args.rm_vw;
+      row_ok = xv < args.rm_ow && line < args.rm_vrows;
+      row = line * args.rm_ow + xv;
     }
     const int col0 = w.nt * BN;
 

@@ -28,6 +28,9 @@ struct mm4_conv_plan {
   bool x_tma_shape;  // stride 1 and 16-byte channel pitch: activations by TMA
   int a_mode;        // CONV_A_IM2COL or CONV_A_RECT on the TMA path
   bool pair;         // im2col path on 2-CTA clusters (256-pixel tiles)
+  bool taprow;       // pair path reading all kw taps from one box per (kd, kh, slab)
+  int vw;            // taprow: virtual row width OW + KW - 1
+  long long m_virtual;  // taprow: N * OD * OH * vw tile rows
   int tw, th;        // output rectangle per tile on the rectangle path (tw * th = 128)
   int tiles_w, tiles_h;
   char name[96];
@@ -72,9 +75,19 @@ mm4_status finish_plan(mm4_conv_plan* p) {
   // CTA pairs on the im2col path (MM4_CONV_PAIR=0 keeps one-CTA tiles).
   const char* pair_env = std::getenv("MM4_CONV_PAIR");
   p->pair = p->x_tma_shape && p->a_mode == CONV_A_IM2COL && !(pair_env && pair_env[0] == '0');
+  // Tap rows on the pair path (MM4_CONV_TAPREUSE=0 keeps one box per tap):
+  // dilation-1 filters 2 or 3 taps wide, with the widened window box's
+  // upper W corner still in 5 bits signed.
+  p->vw = g.OW + g.KW - 1;
+  p->m_virtual = static_cast<long long>(g.N) * g.OD * g.OH * p->vw;
+  const int vw_upper = p->vw - g.PL - g.W;
+  const char* tap_env = std::getenv("MM4_CONV_TAPREUSE");
+  p->taprow = p->pair && g.DX == 1 && g.KW >= 2 && g.KW <= CONV_ROW_MAX_KW && vw_upper >= -16 && vw_upper <= 15 &&
+              p->m_virtual <= (1ll << 31) - 512 && !(tap_env && tap_env[0] == '0');
   snprintf(p->name, sizeof(p->name), "conv_sm100%s<BN=%d,%s,%s>", p->pair ? "_pair" : "", p->bn,
            p->w_tma_shape ? (p->w_mn ? "W:tma-MN" : "W:tma-K") : "W:gather",
-           p->x_tma_shape ? (p->a_mode == CONV_A_IM2COL ? "X:tma-im2col" : "X:tma-rect")
+           p->x_tma_shape ? (p->a_mode == CONV_A_IM2COL ? (p->taprow ? "X:tma-im2col-taprow" : "X:tma-im2col")
+                                                       : "X:tma-rect")
                           : (g.C % 8 == 0) ? "X:cp.async16" : "X:gather16");
   return MM4_OK;
 }
@@ -92,11 +105,11 @@ mm4_status launch(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& 
   return MM4_OK;
 }
 
-template <int BN, bool B_MN>
+template <int BN, bool B_MN, bool TAPROW>
 mm4_status launch_pair(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& args, const ConvGeom& g,
                        int grid, cudaStream_t st) {
-  auto kern = conv_sm100_pair_kernel<BN, B_MN>;
-  constexpr int smem = ConvPairCfg<BN>::SMEM_BYTES;
+  auto kern = conv_sm100_pair_kernel<BN, B_MN, TAPROW>;
+  constexpr int smem = ConvPairCfg<BN, TAPROW>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (rc != MM4_OK) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -291,6 +304,7 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   const bool xtma = tma && p->x_tma_shape && aligned16(x);
   const int amode = xtma ? p->a_mode : CONV_A_GATHER;
   const bool pair = xtma && p->pair;
+  const bool taprow = pair && p->taprow;
   CUtensorMap tx;
   memset(&tx, 0, sizeof(tx));
   if (xtma) {  // NDHWC activations
@@ -301,10 +315,14 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
                                  static_cast<uint64_t>(g.D) * g.H * g.W * g.C * 2};
     if (amode == CONV_A_IM2COL) {
       // Window box of output pixel (ox, oy, oz): input origin (ox - PL, ...);
-      // the box walks origins [-PL, W - 1 + (OW - PL - W)] = OW positions.
+      // the box walks origins [-PL, W - 1 + (OW - PL - W)] = OW positions
+      // per row (tap rows: vw = OW + KW - 1 positions, and KW - 1 more pixels
+      // per box).
+      const int row_w = taprow ? p->vw : g.OW;
       const int lower[3] = {-g.PL, -g.PT, -g.PF};
-      const int upper[3] = {g.OW - g.PL - g.W, g.OH - g.PT - g.H, g.OD - g.PF - g.D};
-      rc = encode_im2col(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, lower, upper, 64, GEMM_BM,
+      const int upper[3] = {row_w - g.PL - g.W, g.OH - g.PT - g.H, g.OD - g.PF - g.D};
+      const int pixels = taprow ? GEMM_BM + g.KW - 1 : GEMM_BM;
+      rc = encode_im2col(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, x, dims, strides, lower, upper, 64, pixels,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     } else {  // box {64 ch, TW, TH, 1, 1}
       const uint32_t box[5] = {64, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1, 1};
@@ -330,10 +348,19 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
     args.num_m_tiles = g.N * g.OD * p->tiles_h * p->tiles_w;
   }
   if (pair) args.num_m_tiles = static_cast<int>((p->m_total + 2 * GEMM_BM - 1) / (2 * GEMM_BM));
+  args.kb_total = g.taps * g.ncb;
+  if (taprow) {
+    args.M = static_cast<int>(p->m_virtual);
+    args.rowmap = 2;
+    args.rm_vw = p->vw;
+    args.rm_vrows = g.N * g.OD * g.OH;
+    args.rm_ow = g.OW;
+    args.num_m_tiles = static_cast<int>((p->m_virtual + 2 * GEMM_BM - 1) / (2 * GEMM_BM));
+    args.kb_total = g.KD * g.KH * g.ncb;  // one k-block per (kd, kh, slab), KW taps each
+  }
   args.num_n_tiles = p->num_n_tiles;
   args.num_tiles = args.num_m_tiles * p->num_n_tiles;
   args.splits = 1;
-  args.kb_total = g.taps * g.ncb;
   args.num_units = args.num_tiles;
   args.group_m = 16;
   args.bias = p->bias ? static_cast<const __half*>(bias) : nullptr;
@@ -342,11 +369,20 @@ mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, co
   args.timeout_ns = wait_timeout_ns();
   const int grid = pair ? 2 * std::min(args.num_units, info.sm_count / 2) : std::min(args.num_units, info.sm_count);
   for (int i = 0; i < duplicated_count; ++i) {
-    if (pair) {
+    if (taprow) {
       if (p->bn == 256)
-        rc = p->w_mn ? launch_pair<256, true>(tm, tx, args, g, grid, st) : launch_pair<256, false>(tm, tx, args, g, grid, st);
+        rc = p->w_mn ? launch_pair<256, true, true>(tm, tx, args, g, grid, st)
+                     : launch_pair<256, false, true>(tm, tx, args, g, grid, st);
       else
-        rc = p->w_mn ? launch_pair<128, true>(tm, tx, args, g, grid, st) : launch_pair<128, false>(tm, tx, args, g, grid, st);
+        rc = p->w_mn ? launch_pair<128, true, true>(tm, tx, args, g, grid, st)
+                     : launch_pair<128, false, true>(tm, tx, args, g, grid, st);
+    } else if (pair) {
+      if (p->bn == 256)
+        rc = p->w_mn ? launch_pair<256, true, false>(tm, tx, args, g, grid, st)
+                     : launch_pair<256, false, false>(tm, tx, args, g, grid, st);
+      else
+        rc = p->w_mn ? launch_pair<128, true, false>(tm, tx, args, g, grid, st)
+                     : launch_pair<128, false, false>(tm, tx, args, g, grid, st);
     } else {
       rc = (p->bn == 256) ? launch_bn<256>(tma, p->w_mn, amode, tm, tx, args, g, grid, st)
                           : launch_bn<128>(tma, p->w_mn, amode, tm, tx, args, g, grid, st);

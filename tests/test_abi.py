@@ -99,6 +99,35 @@ def test_conv_and_attention_plan_validation():
     assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == _lib.MM4_ERR_UNSUPPORTED
 
 
+def test_conv_tap_row_dispatch(monkeypatch):
+    """Stride-1 convs on the CTA-pair path with dilation-1 filters 2 or 3 taps wide read all kw taps
+    from one activation box (kernel name "taprow"); MM4_CONV_TAPREUSE=0 turns it off."""
+    lib = _lib.lib()
+
+    def name2d(*dims):
+        h = ctypes.c_void_p()
+        assert lib.mm4_conv2d_plan_create(ctypes.byref(h), ctypes.byref(_lib.Conv2dDesc(*dims))) == 0
+        n = lib.mm4_conv_plan_kernel_name(h)
+        lib.mm4_conv_plan_destroy(h)
+        return n
+
+    base = (32, 56, 56, 256, 256, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_OHWI, 1)
+    assert b"taprow" in name2d(*base)
+    assert b"taprow" in name2d(*base[:5], 2, 2, *base[7:])            # KW = 2
+    assert b"taprow" not in name2d(*base[:5], 1, 1, *base[7:])        # KW = 1: nothing to share
+    assert b"taprow" not in name2d(*base[:5], 5, 5, *base[7:])        # KW > 3: stage holds 3 taps
+    assert b"taprow" not in name2d(*base[:10], 2, *base[11:])         # dilation 2 in W
+    assert b"taprow" not in name2d(*base[:7], 2, 2, *base[9:])        # stride 2: no TMA activations
+    h = ctypes.c_void_p()
+    d3 = _lib.Conv3dDesc(8, 16, 64, 64, 128, 128, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_ODHWI, 1)
+    assert lib.mm4_conv3d_plan_create(ctypes.byref(h), ctypes.byref(d3)) == 0
+    assert b"taprow" in lib.mm4_conv_plan_kernel_name(h)
+    lib.mm4_conv_plan_destroy(h)
+    monkeypatch.setenv("MM4_CONV_TAPREUSE", "0")
+    n = name2d(*base)
+    assert b"taprow" not in n and b"tma-im2col" in n and b"pair" in n
+
+
 def test_no_device_means_not_supported():
     import torch
     if torch.cuda.is_available():

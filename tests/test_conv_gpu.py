@@ -168,6 +168,46 @@ def test_stride1_activation_paths(cuda, mode, monkeypatch):
     assert_close(got, ref, f"conv3d stride 1 {plan.kernel_name}")
 
 
+TAP_ROW_2D = [
+    # (dims, x seed) -- KW 3 with left-only padding, ragged channel slab, BN 256 (O = 136)
+    Conv2DDimensions(3, 19, 21, 72, 136, 3, 3, 1, 1, 1, 1, 1, 0, 2, 0),
+    # KW 2, right padding only, one channel slab
+    Conv2DDimensions(2, 17, 30, 32, 48, 2, 2, 1, 1, 1, 1, 1, 0, 0, 1),
+    # dilated in H only (tap rows need dilation 1 in W)
+    Conv2DDimensions(2, 15, 13, 24, 40, 3, 3, 1, 1, 2, 1, 2, 2, 1, 1),
+]
+
+
+@pytest.mark.parametrize("taprow", [True, False])
+@pytest.mark.parametrize("idx", range(len(TAP_ROW_2D)))
+def test_tap_rows(cuda, idx, taprow, monkeypatch):
+    """Pair-path convs whose KW taps all read one activation box per (kd, kh,
+    channel slab) (default), against one box per tap (MM4_CONV_TAPREUSE=0):
+    virtual rows OW + KW - 1 wide, the overhang columns dropped in the
+    epilogue, tiles crossing rows and images, ragged last tile."""
+    if taprow:
+        monkeypatch.delenv("MM4_CONV_TAPREUSE", raising=False)
+    else:
+        monkeypatch.setenv("MM4_CONV_TAPREUSE", "0")
+    d = TAP_ROW_2D[idx]
+    x = data.normal((d.batchSize, d.inputHeight, d.inputWidth, d.inputChannels), 1.0, 30 + idx, 0)
+    w = data.normal((d.kernelHeight, d.kernelWidth, d.inputChannels, d.outputChannels), 0.05, 30 + idx, 1)
+    b = data.uniform((d.outputChannels,), -0.1, 0.1, 30 + idx, 2)
+    for layout in (WEIGHTS_HWIO, WEIGHTS_OHWI):
+        plan, got, ref = _run2d(cuda, d, x, w, b, layout=layout)
+        assert ("taprow" in plan.kernel_name) == taprow, plan.kernel_name
+        assert_close(got, ref, f"conv2d tap rows case {idx} {plan.kernel_name}")
+    if idx == 0:
+        d3 = Conv3DDimensions(2, 5, 9, 11, 16, 24, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0)
+        x3 = data.normal((2, 5, 9, 11, 16), 1.0, 9, 0)
+        w3 = data.normal((3, 3, 3, 16, 24), 0.03, 9, 1)
+        b3 = data.uniform((24,), -0.1, 0.1, 9, 2)
+        for layout in (WEIGHTS_DHWIO, WEIGHTS_ODHWI):
+            plan, got, ref = _run3d(cuda, d3, x3, w3, b3, layout=layout)
+            assert ("taprow" in plan.kernel_name) == taprow, plan.kernel_name
+            assert_close(got, ref, f"conv3d tap rows {plan.kernel_name}")
+
+
 def test_baseline_config4_conv2d(cuda):
     """N=32, 56x56, 256->256, 3x3, pad 1, OHWI weights
     N(0,0.05), bias U[-0.1,0.1]. Oracle on a row sample; every output checked
