@@ -40,7 +40,9 @@ class BuildOptions:
 
 
 class AttentionPlan:
-    """Non-causal flash-attention forward for one (batch, dims, layout)."""
+    """Non-causal flash attention for one (batch, dims, layout): the forward (`run`, optionally with the
+    per-row log-sum-exp) and the backward (`backward`: dQ, dK, dV of the loss sum(dO * O), the GPU form of
+    Network.swift derivativeQ / derivativeK / derivativeV, :328-401)."""
 
     def __init__(self, dims: AttentionDimensions, batch: int = 1, layout: int = MM4_ATTN_BHSD,
                  scale: float | None = None, blockDimensions: BlockDimenions | None = None,
@@ -71,15 +73,54 @@ class AttentionPlan:
         """4*B*Hq*R*C*D (two GEMMs); the reference counts (2D+5)*S^2*H (attention.swift:513)."""
         return 4.0 * self.batch * self.dims.Hq * self.dims.R * self.dims.C * self.dims.K
 
-    def run(self, Q, K, V, O=None, stream=None, duplicatedCount: int = 1):
+    def _check(self, **tensors):
         import torch
         d = self.dims
-        for t, shp, n in ((Q, self.shape(d.R, d.Hq), "Q"), (K, self.shape(d.C, d.Hk), "K"),
-                          (V, self.shape(d.C, d.Hk), "V")):
+        shapes = {"Q": self.shape(d.R, d.Hq), "O": self.shape(d.R, d.Hq), "dO": self.shape(d.R, d.Hq),
+                  "K": self.shape(d.C, d.Hk), "V": self.shape(d.C, d.Hk)}
+        for n, t in tensors.items():
+            shp = shapes[n]
             if tuple(t.shape) != shp or t.dtype != torch.float16 or not t.is_cuda or not t.is_contiguous():
                 raise ValueError(f"{n} must be a contiguous CUDA fp16 tensor of shape {shp}")
+
+    def lse_shape(self):
+        return (self.batch, self.dims.Hq, self.dims.R)
+
+    def run(self, Q, K, V, O=None, stream=None, duplicatedCount: int = 1, lse=None):
+        """O = softmax(scale Q K^T) V. With `lse` (fp32 [B][Hq][R] CUDA tensor) also writes each row's
+        natural-log sum of exp(scale * S) (Network.swift createLTerm), which `backward` takes."""
+        import torch
+        d = self.dims
+        self._check(Q=Q, K=K, V=V)
         if O is None:
             O = torch.empty(self.shape(d.R, d.Hq), dtype=torch.float16, device=Q.device)
+        if lse is not None:
+            if tuple(lse.shape) != self.lse_shape() or lse.dtype != torch.float32 or not lse.is_contiguous():
+                raise ValueError(f"lse must be a contiguous fp32 tensor of shape {self.lse_shape()}")
+            if duplicatedCount != 1:
+                raise ValueError("duplicatedCount must be 1 when lse is requested")
+            _lib.check(self._L.mm4_attention_fwd_lse(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                                     O.data_ptr(), lse.data_ptr(), _lib.stream_handle(stream)))
+            return O
         _lib.check(self._L.mm4_attention_fwd(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
                                              _lib.stream_handle(stream), int(duplicatedCount)))
         return O
+
+    def backward(self, Q, K, V, O, dO, lse, stream=None, dQ=None, dK=None, dV=None, workspace=None):
+        """dQ, dK, dV (fp16, the layouts of Q, K, V) of sum(dO * O), from the forward's O and lse."""
+        import torch
+        d = self.dims
+        self._check(Q=Q, K=K, V=V, O=O, dO=dO)
+        if tuple(lse.shape) != self.lse_shape() or lse.dtype != torch.float32 or not lse.is_contiguous():
+            raise ValueError(f"lse must be a contiguous fp32 tensor of shape {self.lse_shape()}")
+        dQ = torch.empty_like(Q) if dQ is None else dQ
+        dK = torch.empty_like(K) if dK is None else dK
+        dV = torch.empty_like(V) if dV is None else dV
+        ws_bytes = self._L.mm4_attention_bwd_workspace_size(self._h)
+        if workspace is None:
+            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=Q.device)
+        _lib.check(self._L.mm4_attention_bwd(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                             dO.data_ptr(), lse.data_ptr(), dQ.data_ptr(), dK.data_ptr(),
+                                             dV.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                                             _lib.stream_handle(stream)))
+        return dQ, dK, dV

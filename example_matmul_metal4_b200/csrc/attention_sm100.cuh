@@ -42,6 +42,7 @@ struct AttnArgs {
   int layout;                           // 0: [B][H][S][D], 1: [B][S][H][D]
   float scale_log2;                     // scale * log2(e)
   __half* O;
+  float* lse;                           // optional [B][Hq][R]: natural-log sum of exp(scale * S) per row
   int* status;
   unsigned long long timeout_ns;
 };
@@ -413,6 +414,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tc_fence_after();
         const int row = blockIdx.x * ATT_CTA_ROWS + ti * ATT_BM + r;
         const float inv_l = 1.0f / l;
+        if (args.lse != nullptr && row < args.R) {
+          // m and l share the same (possibly stale) max, so m + log2(l) is
+          // the row's log2-sum-exp2 of scale*log2(e)*S; times ln 2 gives the
+          // natural-log value (Network.swift createLTerm).
+          args.lse[(static_cast<long long>(b) * args.heads_q + h) * args.R + row] =
+              (m + log2f(l)) * 0.6931471805599453f;
+        }
         __half* dst = nullptr;
         if (row < args.R) {
           const long long off = (args.layout == 0)

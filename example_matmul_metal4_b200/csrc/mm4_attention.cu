@@ -1,10 +1,12 @@
 // Attention plans and dispatch: replaces the reference's attention
 // createSource + run(...) (Sources/attention/attention.swift:23-382, :398-541).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <new>
 
+#include "attention_bwd_sm100.cuh"
 #include "attention_sm100.cuh"
 #include "mm4_internal.h"
 
@@ -68,8 +70,12 @@ void mm4_attention_plan_destroy(mm4_attention_plan* plan) { delete plan; }
 
 const char* mm4_attention_plan_kernel_name(const mm4_attention_plan* plan) { return plan ? plan->name : ""; }
 
-mm4_status mm4_attention_fwd(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, void* O,
-                             mm4_stream_t stream, int duplicated_count) {
+}  // extern "C"
+
+namespace {
+
+mm4_status attention_forward(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, void* O,
+                             float* lse, cudaStream_t st, int duplicated_count) {
   if (!p) return fail(MM4_ERR_INVALID, "null plan");
   if (!Q || !K || !V || !O) return fail(MM4_ERR_INVALID, "null Q/K/V/O pointer");
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
@@ -97,6 +103,7 @@ mm4_status mm4_attention_fwd(const mm4_attention_plan* p, const void* Q, const v
   args.layout = d.layout;
   args.scale_log2 = p->scale * 1.4426950408889634f;
   args.O = static_cast<__half*>(O);
+  args.lse = lse;
   args.status = status;
   args.timeout_ns = wait_timeout_ns();
 
@@ -118,12 +125,106 @@ mm4_status mm4_attention_fwd(const mm4_attention_plan* p, const void* Q, const v
   }
   dim3 grid((d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS, d.heads_q, d.batch);
   if (grid.y > 65535 || grid.z > 65535) return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int i = 0; i < duplicated_count; ++i) {
     attention_fwd_sm100_kernel<<<grid, ATT_THREADS, ATT_SMEM_BYTES, st>>>(tq, tk, tv, args);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "attention_fwd_sm100_kernel launch");
   }
+  return MM4_OK;
+}
+
+int padded_rows(const mm4_attention_desc& d) { return (d.rows + ATT_BM - 1) / ATT_BM * ATT_BM; }
+
+size_t bwd_workspace_bytes(const mm4_attention_desc& d) {
+  return 2 * static_cast<size_t>(d.batch) * d.heads_q * padded_rows(d) * sizeof(float);
+}
+
+}  // namespace
+
+extern "C" {
+
+mm4_status mm4_attention_fwd(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, void* O,
+                             mm4_stream_t stream, int duplicated_count) {
+  return attention_forward(p, Q, K, V, O, nullptr, static_cast<cudaStream_t>(stream), duplicated_count);
+}
+
+mm4_status mm4_attention_fwd_lse(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, void* O,
+                                 float* lse, mm4_stream_t stream) {
+  if (!lse) return fail(MM4_ERR_INVALID, "null lse pointer");
+  return attention_forward(p, Q, K, V, O, lse, static_cast<cudaStream_t>(stream), 1);
+}
+
+size_t mm4_attention_bwd_workspace_size(const mm4_attention_plan* p) { return p ? bwd_workspace_bytes(p->d) : 0; }
+
+mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, const void* O,
+                             const void* dO, const float* lse, void* dQ, void* dK, void* dV, void* workspace,
+                             size_t workspace_bytes, mm4_stream_t stream) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV)
+    return fail(MM4_ERR_INVALID, "null tensor pointer");
+  const void* ptrs[] = {Q, K, V, O, dO, dQ, dK, dV};
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return fail(MM4_ERR_INVALID, "Q, K, V, O, dO, dQ, dK and dV must be 16-byte aligned");
+  const mm4_attention_desc& d = p->d;
+  const size_t need = bwd_workspace_bytes(d);
+  if (!workspace || workspace_bytes < need)
+    return fail(MM4_ERR_WORKSPACE, "attention backward needs a %zu-byte workspace", need);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return fail(MM4_ERR_INVALID, "workspace must be 16-byte aligned");
+  DeviceInfo info;
+  mm4_status rc = current_device(&info);
+  if (rc != MM4_OK) return rc;
+  int* status = nullptr;
+  rc = status_word(&status);
+  if (rc != MM4_OK) return rc;
+  CUtensorMap tq, tk, tv, tdo;
+  rc = encode_attn_map(&tq, Q, d.layout, d.head_dim, d.rows, d.heads_q, d.batch);
+  if (rc == MM4_OK) rc = encode_attn_map(&tdo, dO, d.layout, d.head_dim, d.rows, d.heads_q, d.batch);
+  if (rc == MM4_OK) rc = encode_attn_map(&tk, K, d.layout, d.head_dim, d.columns, d.heads_kv, d.batch);
+  if (rc == MM4_OK) rc = encode_attn_map(&tv, V, d.layout, d.head_dim, d.columns, d.heads_kv, d.batch);
+  if (rc != MM4_OK) return rc;
+
+  const int R_pad = padded_rows(d);
+  float* lse2 = static_cast<float*>(workspace);
+  float* dvec = lse2 + static_cast<size_t>(d.batch) * d.heads_q * R_pad;
+  AttnBwdArgs args{};
+  args.batch = d.batch;
+  args.heads_q = d.heads_q;
+  args.heads_kv = d.heads_kv;
+  args.R = d.rows;
+  args.C = d.columns;
+  args.R_pad = R_pad;
+  args.layout = d.layout;
+  args.scale = p->scale;
+  args.scale_log2 = p->scale * 1.4426950408889634f;
+  args.lse2 = lse2;
+  args.dvec = dvec;
+  args.dQ = static_cast<__half*>(dQ);
+  args.dK = static_cast<__half*>(dK);
+  args.dV = static_cast<__half*>(dV);
+  args.status = status;
+  args.timeout_ns = wait_timeout_ns();
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long rows_total = static_cast<long long>(d.batch) * d.heads_q * R_pad;
+  const int prep_grid = static_cast<int>(std::min<long long>((rows_total + 7) / 8, 16ll * info.sm_count));
+  attention_bwd_prep_kernel<<<prep_grid, 256, 0, st>>>(static_cast<const __half*>(O), static_cast<const __half*>(dO),
+                                                        lse, lse2, dvec, d.batch, d.heads_q, d.rows, R_pad, d.layout);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_prep_kernel launch");
+
+  dim3 grid_kv((d.columns + ATT_BN - 1) / ATT_BN, d.heads_kv, d.batch);
+  dim3 grid_q(R_pad / ATT_BM, d.heads_q, d.batch);
+  if (grid_kv.y > 65535 || grid_kv.z > 65535 || grid_q.y > 65535)
+    return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
+  rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dkdv_kernel), ATB_DKDV_SMEM);
+  if (rc == MM4_OK) rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dq_kernel), ATB_DQ_SMEM);
+  if (rc != MM4_OK) return rc;
+  attention_bwd_dkdv_kernel<<<grid_kv, ATB_THREADS, ATB_DKDV_SMEM, st>>>(tq, tk, tv, tdo, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dkdv_kernel launch");
+  attention_bwd_dq_kernel<<<grid_q, ATB_THREADS, ATB_DQ_SMEM, st>>>(tq, tk, tv, tdo, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dq_kernel launch");
   return MM4_OK;
 }
 

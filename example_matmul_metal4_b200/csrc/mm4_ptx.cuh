@@ -210,6 +210,15 @@ __device__ __forceinline__ void tma_load_5d_im2col(const CUtensorMap* map, uint6
       : "memory");
 }
 
+// Untiled bulk copy global -> shared of `bytes` (a multiple of 16; both
+// addresses 16-byte aligned), completion counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (tcgen05 / TMA) reads of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -210,7 +210,7 @@ MM4_API mm4_status mm4_gemm_splitk_run_distributed(const mm4_gemm_plan* plan, mm
                                                    int duplicated_count);
 
 /* ======================================================================== */
-/* Flash-attention forward                                                  */
+/* Flash-attention forward and backward                                     */
 /* ======================================================================== */
 
 /* Replaces AttentionDimensions / BlockDimenions / BuildOptions + the
@@ -241,6 +241,25 @@ MM4_API void mm4_attention_plan_destroy(mm4_attention_plan* plan);
 MM4_API const char* mm4_attention_plan_kernel_name(const mm4_attention_plan* plan);
 MM4_API mm4_status mm4_attention_fwd(const mm4_attention_plan* plan, const void* Q, const void* K, const void* V, void* O,
                              mm4_stream_t stream, int duplicated_count);
+
+/* Forward that also writes each query row's log-sum-exp, lse[b][h][row] =
+ * log(sum_c exp(scale * S[row][c])) (natural log; Network.swift createLTerm,
+ * :181-203), fp32 [batch][heads_q][rows], for the backward below. */
+MM4_API mm4_status mm4_attention_fwd_lse(const mm4_attention_plan* plan, const void* Q, const void* K, const void* V,
+                                         void* O, float* lse, mm4_stream_t stream);
+
+/* Attention backward. The reference has it only as CPU code
+ * (Network.swift:205-401: derivativeQ / derivativeK / derivativeV of the
+ * loss sum(dO * O)); this is its GPU form. Inputs: Q, K, V, the forward's O
+ * and lse (mm4_attention_fwd_lse), and dO, all in the plan's layout; outputs
+ * dQ, dK, dV (fp16, same layouts as Q, K, V; with heads_kv < heads_q, dK and
+ * dV sum over the query heads sharing a key/value head). workspace: at least
+ * mm4_attention_bwd_workspace_size(plan) bytes, 16-byte aligned, any
+ * contents. Three stream-ordered launches. */
+MM4_API size_t mm4_attention_bwd_workspace_size(const mm4_attention_plan* plan);
+MM4_API mm4_status mm4_attention_bwd(const mm4_attention_plan* plan, const void* Q, const void* K, const void* V,
+                                     const void* O, const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                                     void* workspace, size_t workspace_bytes, mm4_stream_t stream);
 
 /* ======================================================================== */
 /* Convolution (implicit GEMM)                                              */

@@ -229,6 +229,107 @@ void mm4o_attention(int batch, int heads_q, int heads_kv, int R, int C, int D, f
   }
 }
 
+/*
+ * Attention gradients of the loss sum(dO * O) (Network.swift:313-326) for
+ * every (batch, key/value head), following Network.swift:
+ *   createLTerm (:181-203): lse = max + log(sum exp(value - max)), value = scale * S;
+ *   createMatrixPRow (:151-179): P = exp(value - lse);
+ *   createDTerm (:258-282): O = P V (columns ascending), D = O . dO;
+ *   createDerivativePRow (:205-218): dP = dO V^T (d ascending);
+ *   createDerivativeSRow (:220-256): dS = P (dP - D) * scale;
+ *   derivativeQ (:375-401): dQ row = dS K (columns ascending);
+ *   derivativeK (:351-373): dK[c] += dS[c] * q (rows ascending);
+ *   derivativeV (:328-350): dV[c] += P[c] * dO row (rows ascending).
+ * Grouped-query heads: the query heads sharing a key/value head are taken in
+ * ascending order, so dK / dV sum over them. dQ, dK, dV are written with the
+ * element offsets of Q, K, V (same layout, fp32); lse is [batch][heads_q][R].
+ * scratch: threads * (2 * C + D) floats.
+ */
+void mm4o_attention_bwd(int batch, int heads_q, int heads_kv, int R, int C, int D, float scale, int layout,
+                        const uint16_t* Q, const uint16_t* K, const uint16_t* V, const uint16_t* dO, float* dQ,
+                        float* dK, float* dV, float* lse_out, int threads, float* scratch) {
+  set_threads(threads);
+  const int group = heads_q / heads_kv;
+  const int64_t q_rs = layout == 0 ? D : (int64_t)heads_q * D;
+  const int64_t kv_rs = layout == 0 ? D : (int64_t)heads_kv * D;
+#pragma omp parallel for schedule(dynamic, 1) if (threads > 1)
+  for (int bk = 0; bk < batch * heads_kv; ++bk) {
+    int tid = 0;
+#ifdef _OPENMP
+    tid = omp_get_thread_num();
+#endif
+    float* prow = scratch + (int64_t)tid * (2 * C + D);
+    float* dprow = prow + C;
+    float* orow = dprow + C;
+    const int b = bk / heads_kv, hk = bk % heads_kv;
+    const int64_t kv_base = layout == 0 ? ((int64_t)b * heads_kv + hk) * C * D
+                                        : (int64_t)b * C * heads_kv * D + (int64_t)hk * D;
+    const uint16_t* k = K + kv_base;
+    const uint16_t* v = V + kv_base;
+    float* dk = dK + kv_base;
+    float* dv = dV + kv_base;
+    for (int c = 0; c < C; ++c)
+      for (int d = 0; d < D; ++d) {
+        dk[c * kv_rs + d] = 0.0f;
+        dv[c * kv_rs + d] = 0.0f;
+      }
+    for (int g = 0; g < group; ++g) {
+      const int h = hk * group + g;
+      const int64_t q_base = layout == 0 ? ((int64_t)b * heads_q + h) * R * D
+                                         : (int64_t)b * R * heads_q * D + (int64_t)h * D;
+      const uint16_t* q = Q + q_base;
+      const uint16_t* go = dO + q_base;
+      float* dq = dQ + q_base;
+      for (int row = 0; row < R; ++row) {
+        for (int c = 0; c < C; ++c) {
+          float dot = 0.0f;
+          for (int d = 0; d < D; ++d)
+            dot += mm4o_half_to_float(q[row * q_rs + d]) * mm4o_half_to_float(k[c * kv_rs + d]);
+          prow[c] = dot;
+        }
+        float maximum = -3.40282347e+38f;
+        for (int c = 0; c < C; ++c) {
+          const float value = scale * prow[c];
+          maximum = value > maximum ? value : maximum;
+        }
+        float sum = 0.0f;
+        for (int c = 0; c < C; ++c) sum += expf(scale * prow[c] - maximum);
+        const float lse = maximum + logf(sum);
+        lse_out[((int64_t)b * heads_q + h) * R + row] = lse;
+        for (int c = 0; c < C; ++c) prow[c] = expf(scale * prow[c] - lse);
+        for (int d = 0; d < D; ++d) {
+          float dot = 0.0f;
+          for (int c = 0; c < C; ++c) dot += prow[c] * mm4o_half_to_float(v[c * kv_rs + d]);
+          orow[d] = dot;
+        }
+        float term_d = 0.0f;
+        for (int d = 0; d < D; ++d) term_d += orow[d] * mm4o_half_to_float(go[row * q_rs + d]);
+        for (int c = 0; c < C; ++c) {
+          float dot = 0.0f;
+          for (int d = 0; d < D; ++d)
+            dot += mm4o_half_to_float(go[row * q_rs + d]) * mm4o_half_to_float(v[c * kv_rs + d]);
+          dprow[c] = dot;
+        }
+        for (int c = 0; c < C; ++c) {
+          float value = prow[c] * (dprow[c] - term_d);
+          value *= scale;
+          dprow[c] = value; /* dS */
+        }
+        for (int d = 0; d < D; ++d) {
+          float dot = 0.0f;
+          for (int c = 0; c < C; ++c) dot += dprow[c] * mm4o_half_to_float(k[c * kv_rs + d]);
+          dq[row * q_rs + d] = dot;
+        }
+        for (int c = 0; c < C; ++c)
+          for (int d = 0; d < D; ++d) {
+            dk[c * kv_rs + d] += dprow[c] * mm4o_half_to_float(q[row * q_rs + d]);
+            dv[c * kv_rs + d] += prow[c] * mm4o_half_to_float(go[row * q_rs + d]);
+          }
+      }
+    }
+  }
+}
+
 /* ---------------------------------------------------------------- conv */
 
 /* Weight element offset for (oc, kd, kh, kw, ic) in the given layout

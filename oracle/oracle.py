@@ -36,6 +36,8 @@ def lib() -> ctypes.CDLL:
         h.mm4o_gemm.argtypes = [_i, _i, _i, _u16p, _u16p, _u16p, _i, _i, _f32p, _i, _i, _i]
         h.mm4o_attention.argtypes = [_i, _i, _i, _i, _i, _i, ctypes.c_float, _i, _u16p, _u16p, _u16p, _f32p, _i,
                                      _i, _i, _f32p]
+        h.mm4o_attention_bwd.argtypes = [_i, _i, _i, _i, _i, _i, ctypes.c_float, _i, _u16p, _u16p, _u16p, _u16p,
+                                         _f32p, _f32p, _f32p, _f32p, _i, _f32p]
         h.mm4o_conv3d.argtypes = [_i] * 22 + [_u16p, _u16p, _u16p, _f32p, ctypes.c_int64, ctypes.c_int64, _i]
         h.mm4o_permute_weights.argtypes = [_i, _i, _i, _i, _i, _i, _i, _u16p, _u16p]
         h.mm4o_half_to_float.argtypes = [ctypes.c_uint16]
@@ -88,6 +90,22 @@ def attention(Q: np.ndarray, K: np.ndarray, V: np.ndarray, batch: int, heads_q: 
     lib().mm4o_attention(batch, heads_q, heads_kv, R, C, D, float(scale), layout, _h(Q), _h(K), _h(V),
                          out.ctypes.data_as(_f32p), r0, r1, nthreads, scratch.ctypes.data_as(_f32p))
     return out
+
+
+def attention_bwd(Q: np.ndarray, K: np.ndarray, V: np.ndarray, dO: np.ndarray, batch: int, heads_q: int,
+                  heads_kv: int, R: int, C: int, D: int, scale: float, layout: int = 0, threads: int = 1):
+    """fp32 reference of Network.derivativeQ / derivativeK / derivativeV (and createLTerm): returns
+    (dQ, dK, dV, lse) with dQ/dK/dV shaped like Q/K/V and lse shaped (batch, heads_q, R)."""
+    nthreads = max(1, threads)
+    dQ = np.empty(Q.shape, dtype=np.float32)
+    dK = np.empty(K.shape, dtype=np.float32)
+    dV = np.empty(V.shape, dtype=np.float32)
+    lse = np.empty((batch, heads_q, R), dtype=np.float32)
+    scratch = np.empty(nthreads * (2 * C + D), dtype=np.float32)
+    f = lambda a: a.ctypes.data_as(_f32p)  # noqa: E731
+    lib().mm4o_attention_bwd(batch, heads_q, heads_kv, R, C, D, float(scale), layout, _h(Q), _h(K), _h(V), _h(dO),
+                             f(dQ), f(dK), f(dV), f(lse), nthreads, f(scratch))
+    return dQ, dK, dV, lse
 
 
 def conv_out_size(inp: int, pad_lo: int, pad_hi: int, k: int, stride: int, dil: int) -> int:

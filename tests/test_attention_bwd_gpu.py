@@ -1,0 +1,88 @@
+"""Attention backward parity on the GPU: mm4 dQ / dK / dV and the forward's
+log-sum-exp (through the C ABI) vs the C oracle restating Network.swift
+derivativeQ / derivativeK / derivativeV / createLTerm (:181-203, :328-401),
+which tests/test_oracle.py pins against finite differences of the loss."""
+import numpy as np
+import pytest
+
+import oracle
+from example_matmul_metal4_b200 import data, sync_check
+from example_matmul_metal4_b200.attention import MM4_ATTN_BHSD, MM4_ATTN_BSHD, AttentionDimensions, AttentionPlan
+
+pytestmark = pytest.mark.gpu
+
+# Gradients of N(0,1) attention are O(1e-2), below the forward's absolute
+# 2e-2 tolerance, so they are checked relative to their own scale instead:
+# relative Frobenius error <= GRAD_REL_FRO, and every element within
+# GRAD_REL_MAX * max|ref|. fp16 P, dS and outputs carry ~5e-4 relative
+# rounding each.
+GRAD_REL_FRO = 1e-2
+GRAD_REL_MAX = 2e-2
+
+
+def _t(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _check_grad(got, ref, what):
+    g = got.float().cpu().numpy().astype(np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    assert g.shape == r.shape, (what, g.shape, r.shape)
+    rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)
+    worst = float(np.abs(g - r).max())
+    scale = float(np.abs(r).max())
+    assert rel <= GRAD_REL_FRO and worst <= GRAD_REL_MAX * scale, \
+        f"{what}: relative Frobenius error {rel:.3e}, max abs error {worst:.3e}, max |ref| {scale:.3e}"
+
+
+def _forward_backward(cuda, plan, Q, K, V, dO):
+    import torch
+    tQ, tK, tV, tdO = (_t(a, cuda) for a in (Q, K, V, dO))
+    lse = torch.empty(plan.lse_shape(), dtype=torch.float32, device=cuda)
+    O = plan.run(tQ, tK, tV, lse=lse)
+    dQ, dK, dV = plan.backward(tQ, tK, tV, O, tdO, lse)
+    sync_check()
+    return lse, dQ, dK, dV
+
+
+@pytest.mark.parametrize("B,Hq,Hk,R,C,layout", [
+    (1, 2, 2, 256, 256, MM4_ATTN_BHSD),  # whole tiles
+    (2, 4, 2, 200, 333, MM4_ATTN_BSHD),  # grouped-query heads, ragged R and C, [S][H][D] packing
+    (1, 1, 1, 130, 129, MM4_ATTN_BHSD),  # one query row and one key past a tile
+])
+def test_backward_vs_oracle(cuda, B, Hq, Hk, R, C, layout):
+    D = 128
+    plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
+    Q = data.normal(plan.shape(R, Hq), 1.0, 50 + R, 0)
+    K = data.normal(plan.shape(C, Hk), 1.0, 50 + R, 1)
+    V = data.normal(plan.shape(C, Hk), 1.0, 50 + R, 2)
+    dO = data.normal(plan.shape(R, Hq), 1.0, 50 + R, 3)
+    lse, dQ, dK, dV = _forward_backward(cuda, plan, Q, K, V, dO)
+    rQ, rK, rV, rlse = oracle.attention_bwd(Q, K, V, dO, B, Hq, Hk, R, C, D, plan.scale, layout,
+                                            threads=oracle.default_threads())
+    np.testing.assert_allclose(lse.cpu().numpy(), rlse, rtol=1e-4, atol=1e-3, err_msg="lse")
+    _check_grad(dQ, rQ, "dQ")
+    _check_grad(dK, rK, "dK")
+    _check_grad(dV, rV, "dV")
+
+
+def test_backward_full_length_vs_fp32_autograd(cuda):
+    """S = 4096 (the BASELINE sequence length) on two heads: every gradient
+    element against fp32 torch autograd of softmax(scale Q K^T) V on the same
+    fp16 inputs."""
+    import torch
+    B, H, S, D = 1, 2, 4096, 128
+    plan = AttentionPlan(AttentionDimensions(S, S, D, H, H), batch=B)
+    Q, K, V, dO = (data.normal((B, H, S, D), 1.0, 61, i) for i in range(4))
+    lse, dQ, dK, dV = _forward_backward(cuda, plan, Q, K, V, dO)
+    for h in range(H):
+        q, k, v = (_t(a[0, h], cuda).float().requires_grad_(True) for a in (Q, K, V))
+        p = torch.softmax((q @ k.T) * plan.scale, dim=-1)
+        o = p @ v
+        o.backward(_t(dO[0, h], cuda).float())
+        ref_lse = torch.logsumexp((q @ k.T) * plan.scale, dim=-1)
+        np.testing.assert_allclose(lse[0, h].cpu().numpy(), ref_lse.detach().cpu().numpy(), rtol=1e-4, atol=1e-3)
+        _check_grad(dQ[0, h], q.grad.cpu().numpy(), f"dQ h={h}")
+        _check_grad(dK[0, h], k.grad.cpu().numpy(), f"dK h={h}")
+        _check_grad(dV[0, h], v.grad.cpu().numpy(), f"dV h={h}")

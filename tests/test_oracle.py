@@ -138,6 +138,62 @@ def test_attention_oracle_vs_float64(R, C):
                                atol=1e-5)
 
 
+def _bhsd(a, layout):
+    return np.ascontiguousarray(a if layout == 0 else a.transpose(0, 2, 1, 3)).astype(np.float64)
+
+
+def _attention_loss64(Q, K, V, dO, group, scale):
+    """Network.loss (Network.swift:313-326) in float64: sum over heads of dO * softmax(scale Q K^T) V,
+    [B][H][S][D] arrays, query head h reading key/value head h // group."""
+    total = 0.0
+    B, Hq = Q.shape[:2]
+    for b in range(B):
+        for h in range(Hq):
+            s = Q[b, h] @ K[b, h // group].T * scale
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            p /= p.sum(axis=1, keepdims=True)
+            total += float((dO[b, h] * (p @ V[b, h // group])).sum())
+    return total
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_attention_bwd_oracle_vs_finite_differences(layout):
+    """The backward oracle (Network.derivativeQ / derivativeK / derivativeV restated in C, fp32) against
+    central finite differences of the float64 loss, every input element, grouped-query heads (4 query
+    heads on 2 key/value heads), ragged R != C, both layouts; and its LSE against float64 logsumexp."""
+    B, Hq, Hk, R, C, D = 1, 4, 2, 5, 7, 8
+    scale = 1 / np.sqrt(D)
+    shp = (lambda S, H: (B, H, S, D)) if layout == 0 else (lambda S, H: (B, S, H, D))
+    Q = data.normal(shp(R, Hq), 1.0, 41, 0)
+    K = data.normal(shp(C, Hk), 1.0, 41, 1)
+    V = data.normal(shp(C, Hk), 1.0, 41, 2)
+    dO = data.normal(shp(R, Hq), 1.0, 41, 3)
+    dQ, dK, dV, lse = oracle.attention_bwd(Q, K, V, dO, B, Hq, Hk, R, C, D, scale, layout)
+    q, k, v, g = (_bhsd(a, layout) for a in (Q, K, V, dO))
+    group = Hq // Hk
+    eps = 1e-4
+    for name, base, grad in (("Q", q, dQ), ("K", k, dK), ("V", v, dV)):
+        fd = np.zeros_like(base)
+        for idx in np.ndindex(base.shape):
+            args = {"Q": q, "K": k, "V": v}
+            plus, minus = base.copy(), base.copy()
+            plus[idx] += eps
+            minus[idx] -= eps
+            args[name] = plus
+            lp = _attention_loss64(args["Q"], args["K"], args["V"], g, group, scale)
+            args[name] = minus
+            lm = _attention_loss64(args["Q"], args["K"], args["V"], g, group, scale)
+            fd[idx] = (lp - lm) / (2 * eps)
+        np.testing.assert_allclose(_bhsd(grad, layout), fd, rtol=1e-3, atol=2e-4, err_msg=f"d{name}")
+    for b in range(B):
+        for h in range(Hq):
+            s = q[b, h] @ k[b, h // group].T * scale
+            m = s.max(axis=1)
+            ref = m + np.log(np.exp(s - m[:, None]).sum(axis=1))
+            np.testing.assert_allclose(lse[b, h], ref, rtol=1e-5, atol=1e-5)
+
+
 def _conv64(x, w_hwio, bias, pads, strides, dils):
     """NDHWC x [KD][KH][KW][C][O], float64, zero padding."""
     N, D, H, W, C = x.shape
