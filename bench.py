@@ -9,13 +9,16 @@ distributions):
 
   splitk (default)  BASELINE configs[1]: C = A*B + bias, M=N=512, K=65536,
                     split-K 32, fp32 partials reduced in-kernel, fp16 out.
-                    N>1: K is sharded over ranks; each rank computes its fp32
-                    partial, the partials are summed by an NCCL reduce over
-                    NVLink and rank 0 adds bias and rounds (strong scaling).
+                    N>1: every rank holds one K=65536 shard of a problem
+                    with K = 65536*N (weak scaling); the ranks' fp32
+                    partials meet inside the split-K kernels over NVLink
+                    peer memory (one fused launch per GPU, no separate
+                    collective) and rank 0's C holds the result.
   splitk65520       the K=65520 variant of configs[1].
   gemm1024          BASELINE configs[0] (1024^3 GEMM+bias, NN).
   gemm8192          the north-star target shape, 8192^3 GEMM+bias, NN.
   attention         BASELINE configs[2]: B=4, H=16, S=4096, D=128, non-causal.
+  attention_bwd     its backward: dQ, dK, dV from O, dO and the forward's LSE.
   conv2d            BASELINE configs[3]: N=32, 56x56, 256->256, 3x3, pad 1.
   conv3d            BASELINE configs[4]: N=8, D=16, 64x64, 128->128, 3x3x3, pad 1.
   For N>1 the non-split workloads are sharded with no collective: each rank
@@ -125,6 +128,30 @@ class AttentionWorkload:
         return {k: torch.randn(shp, generator=gen, device=dev).half() for k in ("Q", "K", "V")}
 
 
+class AttentionBwdWorkload(AttentionWorkload):
+    """The backward of the attention config: dQ, dK, dV from Q, K, V, the forward's O and LSE, and dO."""
+    name = "attention_bwd_b4_h16_s4096_d128_noncausal"
+
+    def flops(self):
+        # five S-sized GEMMs (S, dP, dV, dK, dQ); the kernels also recompute S and dP once more for dQ
+        return 10.0 * self.B * self.H * self.S * self.S * self.D
+
+    def bytes(self):
+        # Q, K, V, O, dO read and dQ, dK, dV written, fp16; LSE read (fp32)
+        return 8.0 * self.B * self.H * self.S * self.D * 2 + self.B * self.H * self.S * 4
+
+    def config(self):
+        c = super().config()
+        c.update({"workload": self.name, "pass": "backward: dQ, dK, dV of sum(dO * O) (Network.swift:328-401)",
+                  "inputs": "Q, K, V, dO N(0,1) fp16; O and LSE from the forward, outside the timed steps"})
+        return c
+
+    def inputs(self, dev, gen):
+        import torch
+        shp = (self.B, self.H, self.S, self.D)
+        return {k: torch.randn(shp, generator=gen, device=dev).half() for k in ("Q", "K", "V", "dO")}
+
+
 class ConvWorkload:
     def __init__(self, three_d):
         self.three_d = three_d
@@ -176,6 +203,7 @@ WORKLOADS = {
     "gemm1024": lambda: GemmWorkload(1024, 1024, 1024, 1, 1, "tensor", 0),
     "gemm8192": lambda: GemmWorkload(8192, 8192, 8192, 1, 11, "tensor", None),
     "attention": AttentionWorkload,
+    "attention_bwd": AttentionBwdWorkload,
     "conv2d": lambda: ConvWorkload(False),
     "conv3d": lambda: ConvWorkload(True),
 }
@@ -466,6 +494,49 @@ def build_attention(w, dist, dev, gen, l2):
     return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "weak", len(sets)
 
 
+def build_attention_bwd(w, dist, dev, gen, l2):
+    import torch
+    from example_matmul_metal4_b200.attention import AttentionDimensions, AttentionPlan
+    plan = AttentionPlan(AttentionDimensions(w.S, w.S, w.D, w.H, w.H), batch=w.B)
+    t = w.inputs(dev, gen)
+    Q, K, V, dO = t["Q"], t["K"], t["V"], t["dO"]
+    lse = torch.empty(plan.lse_shape(), dtype=torch.float32, device=dev)
+    O = plan.run(Q, K, V, lse=lse)
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    ws = torch.empty(plan._L.mm4_attention_bwd_workspace_size(plan._h), dtype=torch.uint8, device=dev)
+    sets = input_sets({"Q": Q, "K": K, "V": V, "O": O, "dO": dO, "lse": lse}, l2)
+    nxt = cycling(sets)
+
+    def step():
+        t = nxt()
+        plan.backward(t["Q"], t["K"], t["V"], t["O"], t["dO"], t["lse"], dQ=dQ, dK=dK, dV=dV, workspace=ws)
+
+    # torch: SDPA's own backward on a retained graph (its forward runs once, outside the timed steps)
+    q, k, v = (x.detach().clone().requires_grad_(True) for x in (Q, K, V))
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    gq = [None]
+
+    def torch_step():
+        gq[0] = torch.autograd.grad(o, (q, k, v), dO, retain_graph=True)[0]
+    step.comparator = ("torch scaled_dot_product_attention backward (fp16)", torch_step, lambda: dQ,
+                       lambda: gq[0])
+
+    host = {k: v.cpu().pin_memory() for k, v in sets[0].items()}
+    hout = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (dQ, dK, dV)]
+
+    def e2e_step():
+        for k, v in sets[0].items():
+            v.copy_(host[k], non_blocking=True)
+        f = sets[0]
+        plan.backward(f["Q"], f["K"], f["V"], f["O"], f["dO"], f["lse"], dQ=dQ, dK=dK, dV=dV, workspace=ws)
+        for h, d in zip(hout, (dQ, dK, dV)):
+            h.copy_(d, non_blocking=True)
+    h2d = sum(v.numel() * v.element_size() for v in sets[0].values())
+    d2h = 3 * Q.numel() * 2
+    return (step, e2e_step, (h2d, d2h), "attention_bwd_sm100 (prep + dK/dV + dQ kernels)", 3, "weak",
+            len(sets))
+
+
 def build_conv(w, dist, dev, gen, l2):
     import torch
     from example_matmul_metal4_b200.conv import (WEIGHTS_ODHWI, WEIGHTS_OHWI, Conv2DDimensions, Conv3DDimensions,
@@ -521,6 +592,7 @@ def run_mm4(args, w, dist, peaks):
     gen = torch.Generator(device=dev)
     gen.manual_seed(w.seed * 1000003 + dist.rank)
     builder = (build_gemm if isinstance(w, GemmWorkload) else
+               build_attention_bwd if isinstance(w, AttentionBwdWorkload) else
                build_attention if isinstance(w, AttentionWorkload) else build_conv)
     step, e2e_step, e2e_bytes, kernel_name, launches, scaling, nsets = builder(w, dist, dev, gen, args.l2)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if args.l2 == "flush" else None
@@ -621,6 +693,21 @@ def cpu_sample(w, seconds_hint=10.0, threads=None):
         flops = 2.0 * rows * N * K
         sample = (f"{rows} of {M} output rows of the {M}x{N}x{K} GEMM+bias (fp32 loop of matmul.swift:499-510), "
                   f"{dt:.2f} s")
+    elif isinstance(w, AttentionBwdWorkload):
+        S, D = w.S, w.D
+        H = threads  # one head per thread: a block of query rows of each, against all S keys
+        Kt, V = h((1, H, S, D)), h((1, H, S, D))
+
+        def run(rows, heads, nthreads):
+            Qs, dOs = h((1, heads, rows, D)), h((1, heads, rows, D))
+            return timed(lambda: oracle.attention_bwd(Qs, Kt[:, :heads].copy(), V[:, :heads].copy(), dOs, 1, heads,
+                                                      heads, rows, S, D, 1 / math.sqrt(D), threads=nthreads))
+        one = run(1, 1, 1)
+        rows = max(1, min(S, int(seconds_hint / max(one, 1e-6))))
+        dt = run(rows, H, threads)
+        flops = 10.0 * H * rows * S * D
+        sample = (f"{rows} query rows x {H} heads against S={S} keys, D={D} attention backward "
+                  f"(Network.swift:181-401 restated), {dt:.2f} s")
     elif isinstance(w, AttentionWorkload):
         S, D = w.S, w.D
         H = threads  # one head per thread, a block of query rows of each
