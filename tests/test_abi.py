@@ -135,6 +135,35 @@ def test_no_device_means_not_supported():
     assert _lib.lib().mm4_device_supported() == 0
 
 
+def test_attention_backward_sizing_and_validation():
+    """Host-side contract of the attention backward entry points (no device work): the workspace holds
+    the log2-domain LSE and D = rowsum(dO * O) per (batch, query head, row padded to 128), and bad
+    arguments are rejected before any launch."""
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    a = _lib.AttentionDesc(2, 8, 2, 200, 333, 128, 0.0, _lib.MM4_ATTN_BSHD)
+    assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == 0
+    ws = lib.mm4_attention_bwd_workspace_size(h)
+    assert ws == 2 * 2 * 8 * 256 * 4
+    assert lib.mm4_attention_bwd_workspace_size(None) == 0
+    fake = 1 << 20  # 16-byte-aligned stand-ins: every check below fails before a pointer is used
+    ptrs = [fake] * 9  # Q K V O dO lse dQ dK dV
+    assert lib.mm4_attention_bwd(None, *ptrs, fake, ws, None) == _lib.MM4_ERR_INVALID
+    for i in range(9):
+        bad = list(ptrs)
+        bad[i] = None
+        assert lib.mm4_attention_bwd(h, *bad, fake, ws, None) == _lib.MM4_ERR_INVALID
+    bad = list(ptrs)
+    bad[0] = fake + 8
+    assert lib.mm4_attention_bwd(h, *bad, fake, ws, None) == _lib.MM4_ERR_INVALID
+    assert b"aligned" in lib.mm4_last_error()
+    assert lib.mm4_attention_bwd(h, *ptrs, fake, ws - 16, None) == _lib.MM4_ERR_WORKSPACE
+    assert lib.mm4_attention_bwd(h, *ptrs, None, ws, None) == _lib.MM4_ERR_WORKSPACE
+    assert b"workspace" in lib.mm4_last_error()
+    assert lib.mm4_attention_fwd_lse(h, fake, fake, fake, fake, None, None) == _lib.MM4_ERR_INVALID
+    lib.mm4_attention_plan_destroy(h)
+
+
 def test_splitk_group_sizing_and_validation():
     """Host-side checks of the multi-GPU split-K group entry points (no device work)."""
     lib = _lib.lib()
