@@ -503,7 +503,7 @@ def build_attention_bwd(w, dist, dev, gen, l2):
     lse = torch.empty(plan.lse_shape(), dtype=torch.float32, device=dev)
     O = plan.run(Q, K, V, lse=lse)
     dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
-    ws = torch.empty(plan._L.mm4_attention_bwd_workspace_size(plan._h), dtype=torch.uint8, device=dev)
+    ws = torch.empty(plan.backward_workspace_bytes(), dtype=torch.uint8, device=dev)
     sets = input_sets({"Q": Q, "K": K, "V": V, "O": O, "dO": dO, "lse": lse}, l2)
     nxt = cycling(sets)
 

@@ -106,6 +106,10 @@ class AttentionPlan:
                                              _lib.stream_handle(stream), int(duplicatedCount)))
         return O
 
+    def backward_workspace_bytes(self) -> int:
+        """Bytes of scratch `backward` needs (any contents, 16-byte aligned)."""
+        return int(self._L.mm4_attention_bwd_workspace_size(self._h))
+
     def backward(self, Q, K, V, O, dO, lse, stream=None, dQ=None, dK=None, dV=None, workspace=None):
         """dQ, dK, dV (fp16, the layouts of Q, K, V) of sum(dO * O), from the forward's O and lse."""
         import torch
@@ -116,9 +120,8 @@ class AttentionPlan:
         dQ = torch.empty_like(Q) if dQ is None else dQ
         dK = torch.empty_like(K) if dK is None else dK
         dV = torch.empty_like(V) if dV is None else dV
-        ws_bytes = self._L.mm4_attention_bwd_workspace_size(self._h)
         if workspace is None:
-            workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=Q.device)
+            workspace = torch.empty(self.backward_workspace_bytes(), dtype=torch.uint8, device=Q.device)
         _lib.check(self._L.mm4_attention_bwd(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
                                              dO.data_ptr(), lse.data_ptr(), dQ.data_ptr(), dK.data_ptr(),
                                              dV.data_ptr(), workspace.data_ptr(), workspace.numel(),
