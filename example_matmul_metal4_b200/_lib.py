@@ -112,6 +112,7 @@ SIGNATURES = {
     "mm4_conv3d_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(Conv3dDesc)]),
     "mm4_conv_plan_destroy": (None, [_vp]),
     "mm4_conv_plan_kernel_name": (ctypes.c_char_p, [_vp]),
+    "mm4_conv_plan_tile_grid": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int32)]),
     "mm4_conv_output_elements": (ctypes.c_int64, [_vp]),
     "mm4_conv_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int]),
     "mm4_permute_weights": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(_i32), _vp, _vp, _vp]),

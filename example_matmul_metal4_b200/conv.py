@@ -99,6 +99,24 @@ class Conv3DDimensions:
             self.outputChannels * self.kernelDepth * self.kernelHeight * self.kernelWidth * self.inputChannels
 
 
+@dataclass
+class BuildOptions:
+    """The reference's conv BuildOptions (ConvolutionShared.swift:155-185). mm4 chooses its own tiles
+    (128- or 256-pixel implicit-GEMM tiles, see `ConvPlan.tile_grid`); these fields are accepted as
+    tuning hints and recorded in harness reports."""
+    executionSIMDGroups: int = 1
+    outputTileWidth: int | None = None
+    outputTileHeight: int | None = None
+    outputBaseX: int | None = None
+    outputBaseY: int | None = None
+    dispatchGridWidth: int | None = None
+    dispatchGridHeight: int | None = None
+
+    @property
+    def usesOutputTiling(self) -> bool:
+        return self.outputTileWidth is not None and self.outputTileHeight is not None
+
+
 class ConvPlan:
     """A conv2d/conv3d shape + weight layout dispatched to the implicit-GEMM kernel."""
 
@@ -144,6 +162,13 @@ class ConvPlan:
     def handle(self):
         return self._h
 
+    def tile_grid(self) -> tuple[int, int, int]:
+        """Output tiles of the launch (pixel tiles, channel tiles, 1): the analogue of the reference's
+        threadgroup dispatch grid."""
+        g = (ctypes.c_int32 * 3)()
+        _lib.check(self._L.mm4_conv_plan_tile_grid(self._h, g))
+        return (g[0], g[1], g[2])
+
     def run(self, x, w, bias=None, y=None, stream=None, duplicatedCount: int = 1):
         import torch
         if tuple(x.shape) != self.in_shape or x.dtype != torch.float16 or not x.is_cuda or not x.is_contiguous():
@@ -160,11 +185,15 @@ class ConvPlan:
         return y
 
 
-def permute_weights(src, from_layout: int, to_layout: int, dims5, stream=None):
-    """Weight layout transform on the GPU; dims5 = (Cout, Cin, KD, KH, KW)."""
+def permute_weights(src, from_layout: int, to_layout: int, dims5, stream=None, dst=None):
+    """Weight layout transform on the GPU; dims5 = (Cout, Cin, KD, KH, KW). Writes `dst` (same size as
+    src) when given, else a new tensor."""
     import torch
     L = _lib.lib()
-    dst = torch.empty_like(src)
+    if dst is None:
+        dst = torch.empty_like(src)
+    elif dst.numel() != src.numel() or dst.dtype != src.dtype:
+        raise ValueError("dst must match src in size and dtype")
     arr = (ctypes.c_int32 * 5)(*dims5)
     _lib.check(L.mm4_permute_weights(from_layout, to_layout, arr, src.data_ptr(), dst.data_ptr(),
                                      _lib.stream_handle(stream)))

@@ -259,6 +259,18 @@ void mm4_conv_plan_destroy(mm4_conv_plan* plan) { delete plan; }
 
 const char* mm4_conv_plan_kernel_name(const mm4_conv_plan* plan) { return plan ? plan->name : ""; }
 
+mm4_status mm4_conv_plan_tile_grid(const mm4_conv_plan* p, int32_t grid[3]) {
+  if (!p || !grid) return fail(MM4_ERR_INVALID, "null plan or grid");
+  const long long rows = p->taprow ? p->m_virtual : p->m_total;
+  const int tile_m = p->pair ? 2 * GEMM_BM : GEMM_BM;
+  grid[0] = p->a_mode == CONV_A_RECT && p->x_tma_shape && !p->pair
+                ? p->g.N * p->g.OD * p->tiles_h * p->tiles_w
+                : static_cast<int32_t>((rows + tile_m - 1) / tile_m);
+  grid[1] = p->num_n_tiles;
+  grid[2] = 1;
+  return MM4_OK;
+}
+
 int64_t mm4_conv_output_elements(const mm4_conv_plan* plan) {
   return plan ? plan->m_total * plan->g.O : 0;
 }

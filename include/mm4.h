@@ -318,6 +318,13 @@ MM4_API mm4_status mm4_conv2d_plan_create(mm4_conv_plan** plan, const mm4_conv2d
 MM4_API mm4_status mm4_conv3d_plan_create(mm4_conv_plan** plan, const mm4_conv3d_desc* desc);
 MM4_API void mm4_conv_plan_destroy(mm4_conv_plan* plan);
 MM4_API const char* mm4_conv_plan_kernel_name(const mm4_conv_plan* plan);
+/* Output tiles the plan launches over (assuming 16-byte-aligned operands):
+ * grid[0] along output pixels (tiles of 128, or 256 for CTA pairs; virtual
+ * rows OW + KW - 1 wide when the kw taps share one activation box), grid[1]
+ * along output channels, grid[2] = 1. The analogue of the reference's
+ * threadgroup dispatch grid (tensorOpDispatchThreadgroups,
+ * ConvolutionShared.swift:938); host-only. */
+MM4_API mm4_status mm4_conv_plan_tile_grid(const mm4_conv_plan* plan, int32_t grid[3]);
 /* Output element count of the plan (N*OD*OH*OW*Cout). */
 MM4_API int64_t mm4_conv_output_elements(const mm4_conv_plan* plan);
 /* y = conv(x, w) (+ bias). */

@@ -1,20 +1,15 @@
-"""The reference's own validation case lists, restated as data.
+"""The reference's own validation case lists.
 
-conv2d valid cases: ConvolutionHarness.defaultValidationCases
-(ConvolutionShared.swift:2143-2211); padded conv2d probe cases
-(convolution2d_padding.swift:313-388); conv3d cases
-defaultTensorOpConv3DValidationCases (ConvolutionShared.swift:2693-2764) and
-the left/right (H/W) padding cases (:2770-2878).
+conv2d valid cases, conv3d cases and the conv3d left/right (H/W) padding
+cases come from ConvolutionHarness (the defaults of
+ConvolutionShared.swift:2143-2211, :2693-2764, :2770-2878), which restates
+them; the padded conv2d probe cases (convolution2d_padding.swift:313-388) are
+restated here.
 """
-from example_matmul_metal4_b200.conv import Conv2DDimensions, Conv3DDimensions
+from example_matmul_metal4_b200.conv import Conv2DDimensions, Conv3DDimensions  # noqa: F401
+from example_matmul_metal4_b200.harness import ConvolutionHarness
 
-CONV2D_VALID = [
-    Conv2DDimensions(1, 5, 5, 1, 1, 3, 3, 1, 1, 1, 1),
-    Conv2DDimensions(1, 5, 5, 4, 8, 3, 3, 1, 1, 1, 1),
-    Conv2DDimensions(1, 6, 7, 3, 5, 3, 3, 1, 1, 1, 1),
-    Conv2DDimensions(1, 7, 8, 3, 4, 3, 3, 2, 2, 1, 1),
-    Conv2DDimensions(1, 9, 10, 2, 3, 3, 3, 1, 1, 2, 2),
-]
+CONV2D_VALID = ConvolutionHarness.defaultValidationCases()
 
 CONV2D_PADDED = [
     Conv2DDimensions(1, 5, 5, 1, 1, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1),
@@ -23,20 +18,9 @@ CONV2D_PADDED = [
     Conv2DDimensions(1, 33, 35, 4, 8, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1),
 ]
 
-CONV3D_VALID = [
-    Conv3DDimensions(1, 5, 5, 5, 1, 1, 3, 3, 3, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(1, 4, 5, 5, 4, 8, 3, 3, 3, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(2, 7, 6, 7, 3, 5, 3, 3, 3, 2, 1, 1, 1, 1, 1),
-    Conv3DDimensions(1, 7, 7, 7, 2, 3, 3, 3, 3, 1, 1, 1, 2, 2, 2),
-]
+CONV3D_VALID = ConvolutionHarness.defaultTensorOpConv3DValidationCases()
 
-CONV3D_HW_PADDED = [
-    Conv3DDimensions(1, 5, 5, 5, 1, 1, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(1, 4, 5, 5, 4, 8, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(2, 7, 6, 7, 3, 5, 3, 3, 3, 2, 1, 1, 1, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(1, 5, 17, 19, 8, 12, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),
-    Conv3DDimensions(1, 4, 33, 35, 4, 8, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),
-]
+CONV3D_HW_PADDED = ConvolutionHarness.defaultTensorOpConv3DLeftRightPaddingValidationCases()
 
 
 def oracle_kwargs2d(d: Conv2DDimensions):
