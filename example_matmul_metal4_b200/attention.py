@@ -127,3 +127,47 @@ class AttentionPlan:
                                              dV.data_ptr(), workspace.data_ptr(), workspace.numel(),
                                              _lib.stream_handle(stream)))
         return dQ, dK, dV
+
+
+def run(sequenceDimension: int, headDimension: int, Hq: int, Hk: int,
+        buildOptions: BuildOptions | None = None, duplicatedCount: int = 1, seed: int = 3, log=print):
+    """The reference's attention run(sequenceDimension:headDimension:Hq:Hk:buildOptions:duplicatedCount:)
+    (attention.swift:398-541): Q, K, V N(0,1) by Box-Muller (Network.swift:90-129; seeded here) in the
+    [S][H][D] packing; `duplicatedCount` launches; "GFlops" with the reference's (2D+5) S^2 Hq count over
+    their GPU time (:507-515); every element of O checked against the fp32 softmax(Q K^T / sqrt D) V with
+    tolerance 5e-3 (:517-540), the expectation computed by torch on the host. Returns the same record as
+    gemm.run."""
+    import numpy as np
+    import torch
+
+    from . import data
+    from .gemm import RunResult, _check, _gpu_time
+    S, D = sequenceDimension, headDimension
+    plan = AttentionPlan(AttentionDimensions(S, S, D, Hq, Hk), batch=1, layout=MM4_ATTN_BSHD,
+                         buildOptions=buildOptions)
+    Q = data.normal((1, S, Hq, D), 1.0, seed, 0)
+    K = data.normal((1, S, Hk, D), 1.0, seed, 1)
+    V = data.normal((1, S, Hk, D), 1.0, seed, 2)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tQ, tK, tV = (torch.from_numpy(x).to(dev) for x in (Q, K, V))
+    O = torch.empty_like(tQ)
+    seconds = _gpu_time(lambda: plan.run(tQ, tK, tV, O=O), duplicatedCount)
+    ops = (2 * D + 5) * S * S * Hq * duplicatedCount
+    gflops = ops / seconds / 1e9 if seconds > 0 else 0.0
+    log(f"GFlops: {int(gflops)}")
+    q = torch.from_numpy(Q[0]).float().permute(1, 0, 2)                     # [Hq][S][D]
+    k = torch.from_numpy(K[0]).float().permute(1, 0, 2).repeat_interleave(Hq // Hk, dim=0)
+    v = torch.from_numpy(V[0]).float().permute(1, 0, 2).repeat_interleave(Hq // Hk, dim=0)
+    expected = (torch.softmax(q @ k.transpose(1, 2) * plan.scale, dim=-1) @ v).permute(1, 0, 2).numpy()
+    max_err, bad = _check(expected, O[0].float().cpu().numpy(), "O", 5e-3, log)
+    return RunResult(gflops, seconds * 1e3, max_err, bad, plan.kernel_name)
+
+
+def profileCorrectness(sizes=range(1, 1024), log=print):
+    """The reference's sweep (attention.swift:390-395): S = 1..1023, D = 128, Hq = Hk = 8."""
+    out = []
+    for i in sizes:
+        log(f"Problem size: {i}")
+        out.append(run(i, 128, 8, 8, BuildOptions(executionSIMDGroups=16, bypassThreadgroupMemory=True), 1,
+                       log=log))
+    return out

@@ -140,3 +140,83 @@ def _check_tensor(t, shape, name):
         raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
+
+
+@dataclass
+class RunResult:
+    """What the reference's run(...) prints, as a record: GFLOP/s over the GPU time of the launches, and
+    the elements farther than 5e-3 from the fp32 expectation."""
+    gflops: float
+    latencyMS: float
+    maxAbsoluteError: float
+    mismatches: int
+    kernel: str
+
+
+def _gpu_time(launch, duplicatedCount: int) -> float:
+    """Seconds of GPU time of `duplicatedCount` launches (CUDA events around them)."""
+    import torch
+
+    from ._lib import sync_check
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(duplicatedCount):
+        launch()
+    end.record()
+    sync_check()
+    return start.elapsed_time(end) / 1e3
+
+
+def _check(expected, got, name: str, tolerance: float, log) -> tuple[float, int]:
+    import numpy as np
+    err = np.abs(expected - got)
+    bad = np.argwhere(err > tolerance)
+    for idx in bad[:8]:
+        i = tuple(int(v) for v in idx)
+        log(f"CPU calculated {name}{list(i)}: {expected[i]}")
+        log(f"GPU calculated {name}{list(i)}: {got[i]}")
+    return float(err.max()) if err.size else 0.0, int(len(bad))
+
+
+def run(M: int, N: int, K: int, blockDimensions: GEMMDimensions | None = None,
+        buildOptions: BuildOptions | None = None, duplicatedCount: int = 1, seed: int = 1,
+        log=print) -> RunResult:
+    """The reference's matmul run(M:N:K:blockDimensions:buildOptions:duplicatedCount:) (matmul.swift:345-511):
+    A [M][K], B [N][K] (transpose right), bias [N], each U[0,1] * (1/sqrt K) in fp16 (:406-415, seeded here);
+    `duplicatedCount` launches; "GFlops" over their GPU time (:481-489); every element of C checked against
+    the fp32 bias + A B^T with tolerance 5e-3 (:499-510), the expectation computed by torch on the host."""
+    import numpy as np
+    import torch
+
+    from . import data
+    bo = buildOptions or BuildOptions()
+    bo = BuildOptions(bo.cooperativeExecutionSIMDGroups, bo.preemptiveExecutionSIMDGroups, M > N, bo.splitK)
+
+    def scaled(shape, tid):
+        nf = np.float16(1 / np.sqrt(K)).astype(np.float32)
+        return (data.uniform(shape, 0.0, 1.0, seed, tid).astype(np.float32) * nf).astype(np.float16)
+
+    A, B, bias = scaled((M, K), 0), scaled((N, K), 1), scaled((N,), 2)
+    plan = GemmPlan(GEMMDimensions(M, N, K), blockDimensions, transpose=(False, True), bias=True, buildOptions=bo)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tA, tB, tb = (torch.from_numpy(x).to(dev) for x in (A, B, bias))
+    C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    ws = plan.workspace(dev)
+    seconds = _gpu_time(lambda: plan.run(tA, tB, tb, C=C, workspace=ws), duplicatedCount)
+    gflops = 2.0 * M * N * K * duplicatedCount / seconds / 1e9 if seconds > 0 else 0.0
+    log(f"GFlops: {int(gflops)}")
+    expected = (torch.from_numpy(bias).float() + torch.from_numpy(A).float() @ torch.from_numpy(B).float().T).numpy()
+    max_err, bad = _check(expected, C.float().cpu().numpy(), "C", 5e-3, log)
+    return RunResult(gflops, seconds * 1e3, max_err, bad, plan.kernel_name)
+
+
+def profileCorrectness(sizes=range(1, 16385), log=print) -> list[RunResult]:
+    """The reference's square sweep (matmul.swift:337-342): run(i, i, i) with 32x64x64 block hints,
+    1 cooperative / 4 preemptive SIMD groups. The full 1..16384 range checks each size on the host and
+    takes hours; pass a smaller `sizes`."""
+    out = []
+    for i in sizes:
+        log(f"Problem size: {i}")
+        out.append(run(i, i, i, GEMMDimensions(32, 64, 64), BuildOptions(1, 4, True, 1), 1, log=log))
+    return out

@@ -243,3 +243,15 @@ def test_tile_grid_matches_kernel_units():
     # one-CTA gather path (stride 2): 128-pixel tiles over the real output rows
     d = Conv2DDimensions(1, 7, 8, 3, 4, 3, 3, 2, 2, 1, 1)
     assert ConvPlan(d).tile_grid() == (1, 1, 1)
+
+
+def test_driver_check_reports_like_the_reference():
+    from example_matmul_metal4_b200.gemm import _check
+    exp = np.zeros((2, 3), np.float32)
+    got = exp.copy()
+    got[1, 2] = 0.006
+    got[0, 0] = 0.004
+    logs = []
+    worst, bad = _check(exp, got, "C", 5e-3, logs.append)
+    assert bad == 1 and abs(worst - 0.006) < 1e-7
+    assert logs == ["CPU calculated C[1, 2]: 0.0", "GPU calculated C[1, 2]: 0.006000000052154064"]
