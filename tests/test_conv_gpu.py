@@ -5,7 +5,8 @@ import numpy as np
 import pytest
 
 import oracle
-from cases import CONV2D_PADDED, CONV2D_VALID, CONV3D_HW_PADDED, CONV3D_VALID, oracle_kwargs2d, oracle_kwargs3d
+from cases import (CONV2D_PADDED, CONV2D_VALID, CONV3D_HW_PADDED, CONV3D_LR_PADDED, CONV3D_VALID, oracle_kwargs2d,
+                   oracle_kwargs3d)
 from example_matmul_metal4_b200 import data, sync_check
 from example_matmul_metal4_b200.conv import (WEIGHTS_DHWIO, WEIGHTS_HWIO, WEIGHTS_ODHWI, WEIGHTS_OHWI,
                                              WEIGHTS_OIDHW, WEIGHTS_OIHW, Conv2DDimensions, Conv3DDimensions,
@@ -108,6 +109,16 @@ def test_conv3d_reference_padded_cases(cuda, idx, layout):
     if idx == 4:
         # recorded device outcome for N=1 D=4 33x35 C4->8 (AGENTS.md:124): maxAbsoluteError 0.0
         assert v["maxAbsoluteError"] < 2e-2
+
+
+@pytest.mark.parametrize("idx", range(len(CONV3D_LR_PADDED)))
+@pytest.mark.parametrize("layout", [WEIGHTS_DHWIO, WEIGHTS_ODHWI])
+def test_conv3d_left_right_padding_probe(cuda, idx, layout):
+    """The left/right-only padding probe cases (convolution3d_padding.swift:676-742)."""
+    d = CONV3D_LR_PADDED[idx]
+    x, w = _data3d(d)
+    plan, got, ref = _run3d(cuda, d, x, w, layout=layout)
+    assert_close(got, ref, f"conv3d L/R padding probe case {idx} {plan.kernel_name}")
 
 
 def test_conv3d_depth_padding_extension(cuda):

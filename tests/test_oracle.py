@@ -13,7 +13,8 @@ import numpy as np
 import pytest
 
 import oracle
-from cases import CONV2D_PADDED, CONV2D_VALID, CONV3D_HW_PADDED, CONV3D_VALID, oracle_kwargs2d, oracle_kwargs3d
+from cases import (CONV2D_PADDED, CONV2D_VALID, CONV3D_HW_PADDED, CONV3D_LR_PADDED, CONV3D_VALID, oracle_kwargs2d,
+                   oracle_kwargs3d)
 from example_matmul_metal4_b200 import data
 from pathlib import Path
 
@@ -232,7 +233,7 @@ def test_conv2d_oracle_vs_float64_reference_cases(case):
     np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-6)
 
 
-@pytest.mark.parametrize("case", CONV3D_VALID + CONV3D_HW_PADDED)
+@pytest.mark.parametrize("case", CONV3D_VALID + CONV3D_HW_PADDED + CONV3D_LR_PADDED)
 def test_conv3d_oracle_vs_float64_reference_cases(case):
     d = case
     x = data.conv3d_activation(d.batchSize, d.inputDepth, d.inputHeight, d.inputWidth, d.inputChannels)
