@@ -20,3 +20,12 @@ def test_matmul_main_shape(cuda):
 def test_attention_sweep_points(cuda, S):
     r = attention.run(S, 128, 8, 8, attention.BuildOptions(16, True), 1, log=lambda s: None)
     assert r.mismatches == 0, r
+
+
+def test_matmul_profile_correctness_sample(cuda):
+    """Points of the reference's M = N = K sweep (matmul.swift:337-342), its block hints and options:
+    both sides of every power of two up to 512, through the reduced-alignment and tensor-core kernels."""
+    sizes = sorted({1, 2, 3} | {v for p in range(3, 10) for v in (2 ** p - 1, 2 ** p, 2 ** p + 1)})
+    results = gemm.profileCorrectness(sizes=sizes, log=lambda s: None)
+    bad = {n: r for n, r in zip(sizes, results) if r.mismatches}
+    assert not bad, bad
