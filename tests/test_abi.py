@@ -205,3 +205,49 @@ def test_comm_and_peer_argument_checks():
     rc, plan = _gemm(M=512, N=512, K=65536, split_k=32)
     assert lib.mm4_gemm_splitk_run_distributed(plan, None, None, None, None, None, None, 1) == _lib.MM4_ERR_INVALID
     lib.mm4_gemm_plan_destroy(plan)
+
+
+C_PROBE = r"""
+#include "mm4.h"
+#include <stdio.h>
+int main(void) {
+  mm4_gemm_desc d = {512, 512, 65536, 0, 0, 1, 32, 0, 0, 0, 4, 1, 0};
+  mm4_gemm_plan* p = NULL;
+  if (mm4_gemm_plan_create(&p, &d) != MM4_OK) return 1;
+  printf("%s %zu\n", mm4_gemm_plan_kernel_name(p), mm4_gemm_workspace_size(p));
+  mm4_gemm_plan_destroy(p);
+  mm4_conv3d_desc c = {8, 16, 64, 64, 128, 128, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, MM4_WEIGHTS_ODHWI, 1};
+  mm4_conv_plan* cp = NULL;
+  if (mm4_conv3d_plan_create(&cp, &c) != MM4_OK) return 2;
+  int32_t grid[3];
+  if (mm4_conv_plan_tile_grid(cp, grid) != MM4_OK) return 3;
+  printf("%s %d %d %d\n", mm4_conv_plan_kernel_name(cp), grid[0], grid[1], grid[2]);
+  mm4_conv_plan_destroy(cp);
+  return mm4_attention_bwd(NULL, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, NULL) == MM4_ERR_INVALID ? 0 : 4;
+}
+"""
+
+
+def test_header_is_plain_c_and_the_library_links_from_c(tmp_path):
+    """include/mm4.h is a C header (C99, pedantic) and a C program links libmm4.so and calls it --
+    the drop-in boundary as a C or FFI host sees it (host-only calls, no GPU)."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = Path(__file__).resolve().parents[1]
+    inc, libdir = root / "include", root / "example_matmul_metal4_b200"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-fsyntax-only", "-x", "c",
+                    str(inc / "mm4.h")], check=True)
+    src = tmp_path / "probe.c"
+    src.write_text(C_PROBE)
+    exe = tmp_path / "probe"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", f"-I{inc}", str(src), f"-L{libdir}", "-lmm4",
+                    f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    lines = r.stdout.splitlines()
+    assert lines[0].startswith("gemm_sm100_pair<") and "splitk" in lines[0]
+    assert lines[1].endswith("2112 1 1") and "taprow" in lines[1]
