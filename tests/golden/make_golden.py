@@ -56,9 +56,31 @@ def attention_cases():
     return out
 
 
+def attention_bwd_cases():
+    """dQ, dK, dV and the row LSE of the loss sum(dO * O) (Network.swift:181-401 restated)."""
+    out = {}
+    for name, (B, Hq, Hk, R, C, layout, seed) in {
+        "bhsd_1x2_r19_c23": (1, 2, 2, 19, 23, 0, 301),
+        "bshd_1x4_gqa_r12_c17": (1, 4, 2, 12, 17, 1, 302),
+    }.items():
+        D = 128
+        qs = (B, Hq, R, D) if layout == 0 else (B, R, Hq, D)
+        ks = (B, Hk, C, D) if layout == 0 else (B, C, Hk, D)
+        Q = data.normal(qs, 1.0, seed, 0)
+        K = data.normal(ks, 1.0, seed, 1)
+        V = data.normal(ks, 1.0, seed, 2)
+        dO = data.normal(qs, 1.0, seed, 3)
+        dQ, dK, dV, lse = oracle.attention_bwd(Q, K, V, dO, B, Hq, Hk, R, C, D, 1 / np.sqrt(D), layout)
+        out.update({f"{name}/Q": Q, f"{name}/K": K, f"{name}/V": V, f"{name}/dO": dO, f"{name}/dQ": dQ,
+                    f"{name}/dK": dK, f"{name}/dV": dV, f"{name}/lse": lse,
+                    f"{name}/dims": np.array([B, Hq, Hk, R, C, layout])})
+    return out
+
+
 def main():
     np.savez_compressed(HERE / "gemm_small.npz", **gemm_cases())
     np.savez_compressed(HERE / "attention_small.npz", **attention_cases())
+    np.savez_compressed(HERE / "attention_bwd_small.npz", **attention_bwd_cases())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

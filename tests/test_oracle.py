@@ -299,3 +299,17 @@ def test_golden_attention_fixtures():
         got = oracle.attention(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], B, Hq, Hk, R, C, 128, 1 / np.sqrt(128),
                                layout)
         np.testing.assert_allclose(got, z[f"{n}/out"], rtol=1e-6, atol=1e-7)
+
+
+def test_golden_attention_backward_fixtures():
+    """The backward oracle reproduces its committed fixtures (regression pin; the finite-difference test
+    above is the mathematical one)."""
+    z = np.load(GOLDEN / "attention_bwd_small.npz")
+    names = sorted({k.split("/")[0] for k in z.files})
+    assert len(names) == 2
+    for n in names:
+        B, Hq, Hk, R, C, layout = (int(v) for v in z[f"{n}/dims"])
+        got = oracle.attention_bwd(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], z[f"{n}/dO"], B, Hq, Hk, R, C, 128,
+                                   1 / np.sqrt(128), layout)
+        for i, key in enumerate(("dQ", "dK", "dV", "lse")):
+            np.testing.assert_allclose(got[i], z[f"{n}/{key}"], rtol=1e-6, atol=1e-7, err_msg=f"{n} {key}")
