@@ -183,30 +183,35 @@ def run(M: int, N: int, K: int, blockDimensions: GEMMDimensions | None = None,
         buildOptions: BuildOptions | None = None, duplicatedCount: int = 1, seed: int = 1,
         log=print) -> RunResult:
     """The reference's matmul run(M:N:K:blockDimensions:buildOptions:duplicatedCount:) (matmul.swift:345-511):
-    A [M][K], B [N][K] (transpose right), bias [N], each U[0,1] * (1/sqrt K) in fp16 (:406-415, seeded here);
-    `duplicatedCount` launches; "GFlops" over their GPU time (:481-489); every element of C checked against
-    the fp32 bias + A B^T with tolerance 5e-3 (:499-510), the expectation computed by torch on the host."""
+    A [M][K], B [N][K] (transpose right), bias [N], each U[0,1] * (1/sqrt K) in fp16 (:406-415; drawn here on
+    the device from a seeded generator); `duplicatedCount` launches; "GFlops" over their GPU time (:481-489);
+    every element of C checked against bias + A B^T in fp32 with tolerance 5e-3 (:499-510), the expectation
+    formed on the device in fp32 with TF32 off."""
     import numpy as np
     import torch
-
-    from . import data
     bo = buildOptions or BuildOptions()
     bo = BuildOptions(bo.cooperativeExecutionSIMDGroups, bo.preemptiveExecutionSIMDGroups, M > N, bo.splitK)
-
-    def scaled(shape, tid):
-        nf = np.float16(1 / np.sqrt(K)).astype(np.float32)
-        return (data.uniform(shape, 0.0, 1.0, seed, tid).astype(np.float32) * nf).astype(np.float16)
-
-    A, B, bias = scaled((M, K), 0), scaled((N, K), 1), scaled((N,), 2)
-    plan = GemmPlan(GEMMDimensions(M, N, K), blockDimensions, transpose=(False, True), bias=True, buildOptions=bo)
     dev = torch.device("cuda", torch.cuda.current_device())
-    tA, tB, tb = (torch.from_numpy(x).to(dev) for x in (A, B, bias))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    nf = float(np.float16(1 / np.sqrt(K)))
+
+    def scaled(shape):  # fp16(U) * fp16(1/sqrt K), one fp16 rounding of the product, as in Swift's Float16 math
+        return (torch.rand(shape, generator=gen, device=dev).half().float() * nf).half()
+
+    tA, tB, tb = scaled((M, K)), scaled((N, K)), scaled((N,))
+    plan = GemmPlan(GEMMDimensions(M, N, K), blockDimensions, transpose=(False, True), bias=True, buildOptions=bo)
     C = torch.empty((M, N), dtype=torch.float16, device=dev)
     ws = plan.workspace(dev)
     seconds = _gpu_time(lambda: plan.run(tA, tB, tb, C=C, workspace=ws), duplicatedCount)
     gflops = 2.0 * M * N * K * duplicatedCount / seconds / 1e9 if seconds > 0 else 0.0
     log(f"GFlops: {int(gflops)}")
-    expected = (torch.from_numpy(bias).float() + torch.from_numpy(A).float() @ torch.from_numpy(B).float().T).numpy()
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        expected = torch.addmm(tb.float(), tA.float(), tB.float().T).cpu().numpy()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
     max_err, bad = _check(expected, C.float().cpu().numpy(), "C", 5e-3, log)
     return RunResult(gflops, seconds * 1e3, max_err, bad, plan.kernel_name)
 
