@@ -392,7 +392,6 @@ def cycling(sets):
 def build_gemm(w, dist, dev, gen, l2):
     import torch
     from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan
-    from example_matmul_metal4_b200.gemm import splitk_finalize
     P, r = dist.world, dist.rank
     M, N, K = w.M, w.N, w.K
     if P > 1 and w.split > 1:

@@ -137,7 +137,6 @@ def run(sequenceDimension: int, headDimension: int, Hq: int, Hk: int,
     their GPU time (:507-515); every element of O checked against the fp32 softmax(Q K^T / sqrt D) V with
     tolerance 5e-3 (:517-540), the expectation computed by torch on the host. Returns the same record as
     gemm.run."""
-    import numpy as np
     import torch
 
     from . import data

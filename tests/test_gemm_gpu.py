@@ -1,6 +1,5 @@
 """GEMM parity on the GPU: mm4 (through the C ABI) vs the C oracle
 (matmul.swift:499-510 restated), on seeded inputs."""
-import numpy as np
 import pytest
 
 import oracle

@@ -11,12 +11,10 @@ caller workspace) on the same inputs, within the parity tolerance. It lives
 in its own file, collected last, and passes both alone in a fresh process
 and after the other tests.
 """
-import ctypes
 
-import numpy as np
 import pytest
 
-from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan, MM4Error, data, lib, sync_check
+from example_matmul_metal4_b200 import BuildOptions, GEMMDimensions, GemmPlan, data, lib, sync_check
 from example_matmul_metal4_b200._lib import MM4_ERR_INVALID, MM4_ERR_WORKSPACE, check, stream_handle
 from tolerance import assert_close
 
