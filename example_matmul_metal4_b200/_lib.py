@@ -79,6 +79,7 @@ SIGNATURES = {
     "mm4_set_wait_timeout_ns": (None, [ctypes.c_uint64]),
     "mm4_get_wait_timeout_ns": (ctypes.c_uint64, []),
     "mm4_debug_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _vp]),
+    "mm4_debug_ex2": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, ctypes.c_int, _vp]),
     "mm4_workspace_clear": (ctypes.c_int, [_vp, _sz, _vp]),
     "mm4_gemm_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(GemmDesc)]),
     "mm4_gemm_plan_destroy": (None, [_vp]),
@@ -88,6 +89,7 @@ SIGNATURES = {
     "mm4_gemm_partial_run": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mm4_splitk_finalize": (ctypes.c_int, [_i32, _i32, _vp, _vp, _vp, _vp]),
     "mm4_gemm_splitk_run_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "mm4_debug_noalloc_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _vp]),
     "mm4_peer_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_vp), ctypes.POINTER(PeerHandle)]),
     "mm4_peer_free": (ctypes.c_int, [_vp]),
     "mm4_peer_open": (ctypes.c_int, [ctypes.POINTER(PeerHandle), ctypes.POINTER(_vp)]),

@@ -229,3 +229,44 @@ mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const v
 }
 
 }  // extern "C"
+
+namespace {
+
+// Evaluates the forward kernel's two exponentials on a vector: method 0 is
+// the hardware ex2.approx.ftz (MUFU), method 1 the FMA-pipe cubic
+// ex2_poly2 (packed fp32x2: lane x takes x[i], lane y x[i + 1]).
+__global__ void debug_ex2_kernel(const float* x, float* y, long long n, int method) {
+  const long long i = 2 * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float a = x[i];
+  const float b = i + 1 < n ? x[i + 1] : 0.f;
+  float2 r;
+  if (method == 1) {
+    r = ex2_poly2(make_float2(a, b));
+  } else {
+    r.x = ex2_approx(a);
+    r.y = ex2_approx(b);
+  }
+  y[i] = r.x;
+  if (i + 1 < n) y[i + 1] = r.y;
+}
+
+}  // namespace
+
+extern "C" {
+
+mm4_status mm4_debug_ex2(const float* x, float* y, int64_t n, int method, mm4_stream_t stream) {
+  if (n < 0 || (n > 0 && (!x || !y))) return fail(MM4_ERR_INVALID, "mm4_debug_ex2: bad vector");
+  if (method != 0 && method != 1) return fail(MM4_ERR_INVALID, "mm4_debug_ex2: method must be 0 or 1");
+  if (n == 0) return MM4_OK;
+  const long long pairs = (n + 1) / 2;
+  const int threads = 256;
+  const long long blocks = (pairs + threads - 1) / threads;
+  if (blocks > 0x7fffffffLL) return fail(MM4_ERR_INVALID, "mm4_debug_ex2: vector too long");
+  debug_ex2_kernel<<<static_cast<unsigned>(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, y, static_cast<long long>(n), method);
+  MM4_CUDA_TRY(cudaGetLastError());
+  return MM4_OK;
+}
+
+}  // extern "C"

@@ -36,6 +36,15 @@ mm4_status current_device(DeviceInfo* info);
 mm4_status status_word(int** ptr);
 uint64_t wait_timeout_ns();
 
+// Launches the one-warp bounded-wait test kernel on `word` (records
+// MM4_ERR_TIMEOUT at wait site 99 after `timeout_ns`).
+mm4_status launch_debug_wait(int* word, uint64_t timeout_ns, cudaStream_t stream);
+
+// Reads and clears the allocation-free split-K entry point's status words on
+// device `dev` (0 when that entry point never ran there); the caller has
+// synchronised the stream. Defined in mm4_noalloc.cu.
+mm4_status noalloc_take_status(int dev, int* code);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // dependency on libcuda, so the library loads on machines without a GPU).
 mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,

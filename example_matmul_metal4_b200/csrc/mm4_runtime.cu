@@ -182,6 +182,12 @@ __global__ void debug_wait_kernel(int* status, unsigned long long limit_ns) {
   }
 }
 
+mm4_status launch_debug_wait(int* word, uint64_t timeout_ns, cudaStream_t stream) {
+  debug_wait_kernel<<<1, 32, 0, stream>>>(word, timeout_ns);
+  MM4_CUDA_TRY(cudaGetLastError());
+  return MM4_OK;
+}
+
 }  // namespace mm4
 
 using namespace mm4;
@@ -222,13 +228,26 @@ mm4_status mm4_check(mm4_stream_t stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   MM4_CUDA_TRY(cudaStreamSynchronize(st));
   MM4_CUDA_TRY(cudaGetLastError());
+  int dev = -1;
+  MM4_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(MM4_ERR_CUDA, "device id %d out of range", dev);
+  // The library's word exists once a kernel that uses it was launched; before that there is nothing
+  // to read, and mm4_check allocates nothing (callers of the allocation-free entry point rely on it).
   int* word = nullptr;
-  mm4_status rc = status_word(&word);
-  if (rc != MM4_OK) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    word = g_status_words[dev];
+  }
   int v = 0;
-  MM4_CUDA_TRY(cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (word) {
+    MM4_CUDA_TRY(cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) MM4_CUDA_TRY(cudaMemset(word, 0, sizeof(int)));
+  }
+  int nv = 0;
+  mm4_status rc = noalloc_take_status(dev, &nv);
+  if (rc != MM4_OK) return rc;
+  if (v == 0) v = nv;
   if (v != 0) {
-    MM4_CUDA_TRY(cudaMemset(word, 0, sizeof(int)));
     const int code = v & 0xff;
     const int site = v >> 8;
     return fail(code, "device-side error %s recorded at wait site %d", mm4_status_string(code), site);
@@ -243,9 +262,7 @@ mm4_status mm4_debug_wait_timeout(uint64_t timeout_ns, mm4_stream_t stream) {
   int* word = nullptr;
   rc = status_word(&word);
   if (rc != MM4_OK) return rc;
-  debug_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(word, timeout_ns);
-  MM4_CUDA_TRY(cudaGetLastError());
-  return MM4_OK;
+  return launch_debug_wait(word, timeout_ns, static_cast<cudaStream_t>(stream));
 }
 
 mm4_status mm4_workspace_clear(void* workspace, size_t bytes, mm4_stream_t stream) {

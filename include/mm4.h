@@ -54,8 +54,10 @@ MM4_API const char* mm4_last_error(void);
 MM4_API int mm4_device_supported(void);
 
 /* Synchronises `stream`, then reads and clears the current device's status
- * word. Returns MM4_ERR_TIMEOUT when a kernel recorded a run-out wait (the
- * message names the wait site), MM4_ERR_CUDA on a CUDA error, else MM4_OK. */
+ * words: the library's own, and the two of mm4_gemm_splitk_run_noalloc.
+ * Returns MM4_ERR_TIMEOUT when a kernel recorded a run-out wait (the
+ * message names the wait site), MM4_ERR_CUDA on a CUDA error, else MM4_OK.
+ * It allocates no device memory. */
 MM4_API mm4_status mm4_check(mm4_stream_t stream);
 
 /* Upper bound, in nanoseconds, for any single device-side wait (default
@@ -69,6 +71,13 @@ MM4_API uint64_t mm4_get_wait_timeout_ns(void);
  * and the context stays usable. No reference counterpart (the reference
  * calls fatalError on a failed command buffer, ConvolutionShared.swift:955-958). */
 MM4_API mm4_status mm4_debug_wait_timeout(uint64_t timeout_ns, mm4_stream_t stream);
+
+/* Test hook for the attention forward's softmax exponentials: y[i] = 2^x[i]
+ * for i < n (fp32 device vectors) by the hardware ex2.approx (method 0) or
+ * by the kernel's FMA-pipe cubic (method 1; inputs clamped at -125). No
+ * reference counterpart (the reference's softmax uses the Metal exp2,
+ * attention.swift:24). */
+MM4_API mm4_status mm4_debug_ex2(const float* x, float* y, int64_t n, int method, mm4_stream_t stream);
 
 /* Stream-ordered memset to zero (e.g. first-time split-K workspace init). */
 MM4_API mm4_status mm4_workspace_clear(void* workspace, size_t bytes, mm4_stream_t stream);
@@ -144,11 +153,18 @@ MM4_API mm4_status mm4_splitk_finalize(int32_t M, int32_t N, const float* C32, c
  * library (held on every device that loads it until exit); plans whose
  * mm4_gemm_workspace_size() exceeds 4 MiB, or that are not tensor-core
  * split-K plans, are rejected. The first call on a device resolves the
- * array's device address (make it before any stream capture). Each call
- * clears the scratch it uses on `stream`; calls that overlap on the GPU
- * share the scratch and race. */
+ * array's device address (make it before any stream capture; do not use the
+ * entry point across a cudaDeviceReset of that device). Each call clears the
+ * scratch it uses on `stream`; calls that overlap on the GPU share the
+ * scratch and race. A device-side wait that runs out in one call is kept for
+ * mm4_check() (which reports and clears it) and does not affect later calls. */
 MM4_API mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* plan, const void* A, const void* B,
                                                const void* bias, void* C, mm4_stream_t stream);
+/* Test hook for the entry point above: one warp waits, bounded by
+ * `timeout_ns`, on an mbarrier nothing arrives at and records MM4_ERR_TIMEOUT
+ * in the no-alloc status word, as a run-out wait of a no-alloc call would.
+ * No reference counterpart. */
+MM4_API mm4_status mm4_debug_noalloc_wait_timeout(uint64_t timeout_ns, mm4_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Multi-GPU split-K: one process per GPU, fused compute + cross-GPU reduce  */

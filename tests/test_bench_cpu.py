@@ -59,3 +59,26 @@ def test_workload_accounting():
     assert bench.WORKLOADS["splitk"]().bound == "hbm"
     att, bwd = bench.WORKLOADS["attention"](), bench.WORKLOADS["attention_bwd"]()
     assert bwd.flops() == 2.5 * att.flops()
+
+
+def test_strong_scaling_shards_cover_each_named_shape_once():
+    """The N>1 shards split ONE copy of each named shape: K shards on 64-element boundaries for split-K
+    (65536 -> 8 x 8192, 65520 -> 7 x 8192 + 8176), C column blocks for the GEMMs, the 64 (batch, head)
+    units for attention, the batch for conv."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert [bench.shard_range(65536, 8, r, 64) for r in range(8)] == [(8192 * r, 8192) for r in range(8)]
+    assert [bench.shard_range(65520, 8, r, 64)[1] for r in range(8)] == [8192] * 7 + [8176]
+    att = bench.WORKLOADS["attention"]()
+    for parts in (1, 2, 3, 4, 5, 8):
+        for total, align in ((65536, 64), (65520, 64), (1024, 8), (8192, 8), (32, 1), (8, 1), (64, 1)):
+            ranges = [bench.shard_range(total, parts, r, align) for r in range(parts)]
+            assert sum(c for _, c in ranges) == total
+            assert all(s == (ranges[i - 1][0] + ranges[i - 1][1]) for i, (s, _) in enumerate(ranges) if i)
+            assert all(s % align == 0 for s, _ in ranges)
+        units = 0
+        for r in range(parts):
+            nb, nh = att.shard(parts, r)
+            units += nb * nh
+        assert units == att.B * att.H
+    assert att.shard(2, 1) == (2, 16) and att.shard(8, 3) == (1, 8)

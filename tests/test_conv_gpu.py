@@ -106,9 +106,17 @@ def test_conv3d_reference_padded_cases(cuda, idx, layout):
     x, w = _data3d(d)
     plan, got, ref = _run3d(cuda, d, x, w, layout=layout)
     v = assert_close(got, ref, f"conv3d padded case {idx}")
+    # The reference's recorded device outcomes (AGENTS.md:123-124): N=1 D=5 17x19 C8->12 gave
+    # maxAbsoluteError 0.001953125 and N=1 D=4 33x35 C4->8 gave 0.0, both with 0 mismatches. The formula
+    # data are multiples of 1/32, so the fp32 sums are exact and the only error left is the one rounding
+    # to fp16: the kernel's output is the oracle's rounded bit for bit, and the recorded bounds hold as
+    # written.
+    if idx == 3:
+        assert v["maxAbsoluteError"] <= 0.001953125 and v["mismatches"] == 0, v
     if idx == 4:
-        # recorded device outcome for N=1 D=4 33x35 C4->8 (AGENTS.md:124): maxAbsoluteError 0.0
-        assert v["maxAbsoluteError"] < 2e-2
+        assert v["maxAbsoluteError"] == 0.0 and v["mismatches"] == 0, v
+    if idx in (3, 4):
+        np.testing.assert_array_equal(got.astype(np.float16), oracle.to_half(ref))
 
 
 @pytest.mark.parametrize("idx", range(len(CONV3D_LR_PADDED)))
