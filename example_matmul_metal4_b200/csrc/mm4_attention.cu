@@ -53,9 +53,8 @@ mm4_status mm4_attention_plan_create(mm4_attention_plan** out, const mm4_attenti
     return fail(MM4_ERR_INVALID, "heads_kv (%d) must divide heads_q (%d)", d->heads_kv, d->heads_q);
   if (d->layout != MM4_ATTN_BHSD && d->layout != MM4_ATTN_BSHD)
     return fail(MM4_ERR_INVALID, "unknown attention layout %d", d->layout);
-  if (d->head_dim != ATT_D)
-    return fail(MM4_ERR_UNSUPPORTED, "head_dim %d: this build implements head_dim 128 (the reference's D)",
-                d->head_dim);
+  if (d->head_dim != 128 && d->head_dim != 64)
+    return fail(MM4_ERR_UNSUPPORTED, "head_dim %d: this build implements head_dim 128 and 64", d->head_dim);
   if (!(d->scale >= 0.f) && !(d->scale < 0.f)) return fail(MM4_ERR_INVALID, "scale is NaN");
   mm4_attention_plan* p = new (std::nothrow) mm4_attention_plan();
   if (!p) return fail(MM4_ERR_INVALID, "out of host memory");
@@ -73,6 +72,37 @@ const char* mm4_attention_plan_kernel_name(const mm4_attention_plan* plan) { ret
 }  // extern "C"
 
 namespace {
+
+template <int D>
+mm4_status launch_forward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& args,
+                          const mm4_attention_desc& d, cudaStream_t st, int duplicated_count) {
+  const void* kern = reinterpret_cast<const void*>(attention_fwd_sm100_kernel<D>);
+  constexpr int smem = AttFwdCfg<D>::SMEM_BYTES;
+  mm4_status rc = ensure_smem_attr(kern, smem);
+  if (rc != MM4_OK) return rc;
+  {
+    // The kernel moves registers between warpgroups (setmaxnreg); that only
+    // completes if the launch allocates at least ATT_REGS_NEEDED per thread.
+    static int launch_regs = -1;
+    if (launch_regs < 0) {
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(attention_fwd_sm100_kernel)");
+      launch_regs = fa.numRegs;
+    }
+    if (launch_regs < ATT_REGS_NEEDED)
+      return fail(MM4_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs %d", launch_regs,
+                  ATT_REGS_NEEDED);
+  }
+  dim3 grid((d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS, d.heads_q, d.batch);
+  if (grid.y > 65535 || grid.z > 65535) return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
+  for (int i = 0; i < duplicated_count; ++i) {
+    attention_fwd_sm100_kernel<D><<<grid, ATT_THREADS, smem, st>>>(tq, tk, tv, args);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "attention_fwd_sm100_kernel launch");
+  }
+  return MM4_OK;
+}
 
 mm4_status attention_forward(const mm4_attention_plan* p, const void* Q, const void* K, const void* V, void* O,
                              float* lse, cudaStream_t st, int duplicated_count) {
@@ -107,30 +137,8 @@ mm4_status attention_forward(const mm4_attention_plan* p, const void* Q, const v
   args.status = status;
   args.timeout_ns = wait_timeout_ns();
 
-  rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_fwd_sm100_kernel), ATT_SMEM_BYTES);
-  if (rc != MM4_OK) return rc;
-  {
-    // The kernel moves registers between warpgroups (setmaxnreg); that only
-    // completes if the launch allocates at least ATT_REGS_NEEDED per thread.
-    static int launch_regs = -1;
-    if (launch_regs < 0) {
-      cudaFuncAttributes fa;
-      cudaError_t e = cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(attention_fwd_sm100_kernel));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(attention_fwd_sm100_kernel)");
-      launch_regs = fa.numRegs;
-    }
-    if (launch_regs < ATT_REGS_NEEDED)
-      return fail(MM4_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs %d", launch_regs,
-                  ATT_REGS_NEEDED);
-  }
-  dim3 grid((d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS, d.heads_q, d.batch);
-  if (grid.y > 65535 || grid.z > 65535) return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
-  for (int i = 0; i < duplicated_count; ++i) {
-    attention_fwd_sm100_kernel<<<grid, ATT_THREADS, ATT_SMEM_BYTES, st>>>(tq, tk, tv, args);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "attention_fwd_sm100_kernel launch");
-  }
-  return MM4_OK;
+  if (d.head_dim == 128) return launch_forward<128>(tq, tk, tv, args, d, st, duplicated_count);
+  return launch_forward<64>(tq, tk, tv, args, d, st, duplicated_count);
 }
 
 int padded_rows(const mm4_attention_desc& d) { return (d.rows + ATT_BM - 1) / ATT_BM * ATT_BM; }
@@ -160,6 +168,9 @@ mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const v
                              const void* dO, const float* lse, void* dQ, void* dK, void* dV, void* workspace,
                              size_t workspace_bytes, mm4_stream_t stream) {
   if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (p->d.head_dim != ATT_D)
+    return fail(MM4_ERR_UNSUPPORTED, "attention backward: head_dim %d (this build's backward implements 128)",
+                p->d.head_dim);
   if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV)
     return fail(MM4_ERR_INVALID, "null tensor pointer");
   const void* ptrs[] = {Q, K, V, O, dO, dQ, dK, dV};

@@ -16,8 +16,7 @@ def _t(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-def _run(cuda, B, Hq, Hk, R, C, layout=MM4_ATTN_BHSD, seed=3, rows=None):
-    D = 128
+def _run(cuda, B, Hq, Hk, R, C, layout=MM4_ATTN_BHSD, seed=3, rows=None, D=128):
     plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
     Q = data.normal(plan.shape(R, Hq), 1.0, seed, 0)
     K = data.normal(plan.shape(C, Hk), 1.0, seed, 1)
@@ -34,29 +33,49 @@ def _run(cuda, B, Hq, Hk, R, C, layout=MM4_ATTN_BHSD, seed=3, rows=None):
     return plan, got, ref
 
 
+@pytest.mark.parametrize("D", [128, 64])
 @pytest.mark.parametrize("S", [1, 7, 64, 127, 128, 129, 300, 1023])
-def test_reference_sweep_points(cuda, S):
-    """Points of the reference's S = 1..1023, D = 128, Hq = Hk = 8 sweep (attention.swift:391-396)."""
-    plan, got, ref = _run(cuda, 1, 8, 8, S, S)
-    assert_close(got, ref, f"S={S}")
+def test_reference_sweep_points(cuda, S, D):
+    """Points of the reference's S = 1..1023, Hq = Hk = 8 sweep (attention.swift:391-396) at its head
+    dimension 128 and at 64 (run(...) takes headDimension as a parameter, attention.swift:398)."""
+    plan, got, ref = _run(cuda, 1, 8, 8, S, S, D=D)
+    assert_close(got, ref, f"S={S} D={D}")
 
 
+@pytest.mark.parametrize("D", [128, 64])
 @pytest.mark.parametrize("layout", [MM4_ATTN_BHSD, MM4_ATTN_BSHD])
-def test_layouts_and_batch(cuda, layout):
-    plan, got, ref = _run(cuda, 2, 4, 4, 256, 384, layout=layout)
-    assert_close(got, ref, f"layout {layout}")
+def test_layouts_and_batch(cuda, layout, D):
+    plan, got, ref = _run(cuda, 2, 4, 4, 256, 384, layout=layout, D=D)
+    assert_close(got, ref, f"layout {layout} D={D}")
 
 
-def test_gqa_and_rectangular(cuda):
-    plan, got, ref = _run(cuda, 2, 8, 2, 200, 520)
-    assert_close(got, ref, "GQA 8/2, R=200 C=520")
+@pytest.mark.parametrize("D", [128, 64])
+def test_gqa_and_rectangular(cuda, D):
+    plan, got, ref = _run(cuda, 2, 8, 2, 200, 520, D=D)
+    assert_close(got, ref, f"GQA 8/2, R=200 C=520, D={D}")
 
 
-def test_large_logits_rescale_path(cuda):
+def test_repeated_launches_are_bitwise_identical(cuda):
+    """Each output element is one fixed sequence of MMAs and softmax steps: 20 launches of one plan on the
+    same inputs (the reference's duplicatedCount) give the same bits every time."""
+    import torch
+    B, H, S, D = 2, 4, 1024, 128
+    plan = AttentionPlan(AttentionDimensions(S, S, D, H, H), batch=B)
+    Q, K, V = (_t(data.normal((B, H, S, D), 1.0, 13, i), cuda) for i in range(3))
+    first = plan.run(Q, K, V).clone()
+    O = torch.empty_like(first)
+    for _ in range(4):
+        plan.run(Q, K, V, O=O, duplicatedCount=5)
+        sync_check()
+        assert torch.equal(O, first)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_large_logits_rescale_path(cuda, D):
     """Scaled inputs push the running max up across key tiles so the lazy
     rescale of O (max growth > 2^8) is exercised."""
     import torch
-    B, H, R, C, D = 1, 2, 256, 1024, 128
+    B, H, R, C = 1, 2, 256, 1024
     plan = AttentionPlan(AttentionDimensions(R, C, D, H, H), batch=B)
     Q = data.normal((B, H, R, D), 1.0, 8, 0)
     Kn = data.normal((B, H, C, D), 1.0, 8, 1).astype(np.float32)
@@ -66,7 +85,7 @@ def test_large_logits_rescale_path(cuda):
     O = plan.run(_t(Q, cuda), _t(K, cuda), _t(V, cuda))
     sync_check()
     ref = oracle.attention(Q, K, V, B, H, H, R, C, D, plan.scale, 0, threads=oracle.default_threads())
-    assert_close(O.float().cpu().numpy(), ref, "rescale path")
+    assert_close(O.float().cpu().numpy(), ref, f"rescale path D={D}")
 
 
 def test_baseline_config3_rows_sample(cuda):
@@ -91,6 +110,16 @@ def test_baseline_config3_rows_sample(cuda):
         p = torch.softmax(s, dim=-1)
         o = p @ V[b, h].float()
         assert_close(O[b, h].float().cpu().numpy(), o.cpu().numpy(), f"b={b} h={h} vs fp32 torch")
+
+
+def test_head_dim_64_full_length_rows_sample(cuda):
+    """The BASELINE attention shape at head_dim 64 (B=4, H=16, S=4096): oracle rows at both ends of every
+    (b, h)."""
+    B, H, S = 4, 16, 4096
+    plan, got, ref = _run(cuda, B, H, H, S, S, rows=(0, 4), D=64)
+    assert_close(got, ref, "D=64 rows 0:4")
+    plan, got, ref = _run(cuda, B, H, H, S, S, rows=(4093, 4096), D=64)
+    assert_close(got, ref, "D=64 rows 4093:4096")
 
 
 def test_unsupported_head_dim_is_rejected():
