@@ -1,4 +1,4 @@
-// Flash-attention backward (non-causal, head_dim 128) for sm_100a.
+// Flash-attention backward (non-causal, head_dim 128 and 64) for sm_100a.
 //
 // The reference computes these gradients only on the CPU
 // (Sources/attention/Network.swift:205-401): with P = softmax(scale * Q K^T),
@@ -22,17 +22,23 @@
 //                                rows): Q_i, dO_i stay, K_j / V_j stream;
 //                                dQ_i accumulates in TMEM.
 // Both main kernels recompute P from S and the stored LSE rather than
-// reading it. Their tensor-core steps are tcgen05.mma with fp32 TMEM
-// accumulators; the element-wise step (P, dS) runs in four warps, one TMEM
-// lane (one row of S^T or S) per thread, and writes P / dS as fp16 pairs back
-// over the S / dP columns they came from, where the next MMAs read them as
-// their A operand (the forward kernel's P-over-S scheme: the MMAs of one
-// issuing thread execute in issue order, so the next S overwrites P only
-// after the MMAs that read it).
+// reading it. Each streamed 128-row tile is processed as two 64-column
+// halves ("units") through two TMEM buffers, so the tensor core computes one
+// unit's S / dP while an element-wise warpgroup turns the other unit's S / dP
+// into P / dS:
+//   buffer b (units of half b):  S-shaped product in 64 columns, then dP in
+//                                the next 64; the element-wise warpgroup of
+//                                buffer b writes P (or dS) as fp16 pairs over
+//                                the first 32 columns of each, where the
+//                                accumulating MMAs read them as their A
+//                                operand.
+// The next unit of a buffer overwrites those fp16 pairs, so its S / dP MMAs
+// are issued only after the commit of the MMAs that read them has completed
+// (buf_free[b], an mbarrier), never on the strength of issue order.
 //
-// TMEM columns (512), dK/dV kernel: [0,128) S^T then P^T | [128,256) dP^T
-// then dS^T | [256,384) dV | [384,512) dK. dQ kernel: [0,128) S then dS |
-// [128,256) dP | [256,384) dQ.
+// TMEM columns (512), dK/dV kernel: [0,128) buffer 0 | [128,256) buffer 1 |
+// [256,256+D) dV | [256+D,256+2D) dK. dQ kernel: [0,128) buffer 0 |
+// [128,256) buffer 1 | [256,256+D) dQ.
 #pragma once
 
 #include "attention_sm100.cuh"
@@ -53,12 +59,15 @@ struct AttnBwdArgs {
   unsigned long long timeout_ns;
 };
 
-constexpr int ATB_THREADS = 256;  // warp 0 TMA, warp 1 MMA, warps 4-7 element-wise + epilogue
+constexpr int ATB_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4-7 / 8-11 element-wise (buffer 0 / 1)
 constexpr int ATB_STAGES = 2;
 constexpr int ATB_VEC_BYTES = ATT_BM * 4;  // one tile's LSE or D values
-constexpr int ATB_DKDV_SMEM =
-    2 * ATT_TILE_BYTES + ATB_STAGES * (2 * ATT_TILE_BYTES + 2 * ATB_VEC_BYTES) + 256 + 1024;
-constexpr int ATB_DQ_SMEM = 2 * ATT_TILE_BYTES + ATB_STAGES * 2 * ATT_TILE_BYTES + 256 + 1024;
+template <int D>
+struct AtbCfg {
+  static constexpr int TILE_BYTES = 128 * D * 2;  // one 128-row tile of head dim D
+  static constexpr int DKDV_SMEM = 2 * TILE_BYTES + ATB_STAGES * (2 * TILE_BYTES + 2 * ATB_VEC_BYTES) + 256 + 1024;
+  static constexpr int DQ_SMEM = 2 * TILE_BYTES + ATB_STAGES * 2 * TILE_BYTES + 256 + 1024;
+};
 
 enum : int {
   SITE_ATB_PRODUCER = 90,
@@ -69,15 +78,17 @@ enum : int {
   SITE_ATB_MMA_DRAIN = 95,
   SITE_ATB_EW_S = 96,
   SITE_ATB_EW_ACC = 97,
+  SITE_ATB_MMA_FREE = 98,
 };
 
-__device__ __forceinline__ long long attn_row_offset(int layout, int b, int heads, int S, int h, int row) {
-  return layout == 0 ? ((static_cast<long long>(b) * heads + h) * S + row) * ATT_D
-                     : ((static_cast<long long>(b) * S + row) * heads + h) * ATT_D;
+__device__ __forceinline__ long long attn_row_offset(int layout, int b, int heads, int S, int h, int row, int D) {
+  return layout == 0 ? ((static_cast<long long>(b) * heads + h) * S + row) * D
+                     : ((static_cast<long long>(b) * S + row) * heads + h) * D;
 }
 
 // D and the log2-domain LSE for every (batch, query head, padded row); one
-// warp per row.
+// warp per row, D / 32 elements per lane.
+template <int D>
 __global__ void __launch_bounds__(256) attention_bwd_prep_kernel(const __half* __restrict__ O,
                                                                  const __half* __restrict__ dO,
                                                                  const float* __restrict__ lse, float* lse2,
@@ -94,14 +105,13 @@ __global__ void __launch_bounds__(256) attention_bwd_prep_kernel(const __half* _
     const int b = static_cast<int>(bh / heads);
     float dot = 0.f;
     if (row < R) {
-      const long long off = attn_row_offset(layout, b, heads, R, h, row) + lane * 4;
-      const uint2 ov = *reinterpret_cast<const uint2*>(O + off);
-      const uint2 gv = *reinterpret_cast<const uint2*>(dO + off);
-      const float2 o0 = __half22float2(*reinterpret_cast<const __half2*>(&ov.x));
-      const float2 o1 = __half22float2(*reinterpret_cast<const __half2*>(&ov.y));
-      const float2 g0 = __half22float2(*reinterpret_cast<const __half2*>(&gv.x));
-      const float2 g1 = __half22float2(*reinterpret_cast<const __half2*>(&gv.y));
-      dot = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+      const long long off = attn_row_offset(layout, b, heads, R, h, row, D) + lane * (D / 32);
+#pragma unroll
+      for (int k = 0; k < D / 32; k += 2) {
+        const float2 o = __half22float2(*reinterpret_cast<const __half2*>(O + off + k));
+        const float2 g = __half22float2(*reinterpret_cast<const __half2*>(dO + off + k));
+        dot += o.x * g.x + o.y * g.y;
+      }
     }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, s);
@@ -112,20 +122,24 @@ __global__ void __launch_bounds__(256) attention_bwd_prep_kernel(const __half* _
   }
 }
 
-// One 64-column half of a thread's S / dP row pair: P = 2^(s * scale_log2 -
-// lse2), dS = P * (dP - D) * scale, packed as fp16 pairs. Column c uses
-// lse2_of(c) / d_of(c) and is zeroed when !valid(c).
+// One unit of a thread's S / dP row pair (64 columns, two steps of 32):
+// P = 2^(s * scale_log2 - lse2), dS = P * (dP - D) * scale. Column c (0..63
+// of the unit) uses lse2_of(c) / d_of(c) and is zeroed when !valid(c). After
+// each step its fp16 pairs are stored: with want_p, P over the S columns and
+// dS over the dP columns (the dK/dV kernel reads both); without, dS over the
+// S columns (the dQ kernel reads only dS). A step overwrites only columns an
+// earlier step (or itself) has already read.
 template <typename LseF, typename DF, typename ValidF>
-__device__ __forceinline__ void atb_elementwise_half(uint32_t tS, uint32_t tP, int half, float sl2, float scale,
-                                                     LseF lse2_of, DF d_of, ValidF valid, uint32_t (&pp)[32],
-                                                     uint32_t (&pd)[32]) {
+__device__ __forceinline__ void atb_elementwise_unit(uint32_t tS, uint32_t tP, float sl2, float scale, LseF lse2_of,
+                                                     DF d_of, ValidF valid, bool want_p) {
 #pragma unroll
   for (int sub = 0; sub < 2; ++sub) {
-    const int c0 = half * 64 + sub * 32;
+    const int c0 = sub * 32;
     uint32_t vs[32], vp[32];
     tmem_ld_32x32b_x32(tS + c0, vs);
     tmem_ld_32x32b_x32(tP + c0, vp);
     tmem_ld_wait();
+    uint32_t pp[16], pd[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int c = c0 + 2 * e;
@@ -135,16 +149,23 @@ __device__ __forceinline__ void atb_elementwise_half(uint32_t tS, uint32_t tP, i
       if (!valid(c + 1)) p1 = 0.f;
       const float d0 = p0 * (__uint_as_float(vp[2 * e]) - d_of(c)) * scale;
       const float d1 = p1 * (__uint_as_float(vp[2 * e + 1]) - d_of(c + 1)) * scale;
-      pp[sub * 16 + e] = pack_half2(p0, p1);
-      pd[sub * 16 + e] = pack_half2(d0, d1);
+      pp[e] = pack_half2(p0, p1);
+      pd[e] = pack_half2(d0, d1);
+    }
+    if (want_p) {
+      tmem_st_32x32b_x16(tS + sub * 16, pp);
+      tmem_st_32x32b_x16(tP + sub * 16, pd);
+    } else {
+      tmem_st_32x32b_x16(tS + sub * 16, pd);
     }
   }
 }
 
-// Reads a 128-column fp32 accumulator row from TMEM and stores it as fp16.
+// Reads a D-column fp32 accumulator row from TMEM and stores it as fp16.
+template <int D>
 __device__ __forceinline__ void atb_store_row(uint32_t taddr, __half* dst) {
 #pragma unroll 1
-  for (int c = 0; c < ATT_D / 32; ++c) {
+  for (int c = 0; c < D / 32; ++c) {
     uint32_t v[32];
     tmem_ld_32x32b_x32(taddr + c * 32, v);
     tmem_ld_wait();
@@ -162,48 +183,56 @@ __device__ __forceinline__ void atb_store_row(uint32_t taddr, __half* dst) {
   }
 }
 
-// S-shaped MMA (M = 128, N = 128, K = D): D[tmem] = A_tile * B_tile^T, both
-// tiles [128 rows][128 D] as two 64-wide 128-byte-swizzled boxes.
-__device__ __forceinline__ void atb_mma_nt(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
-  constexpr uint32_t IDESC_S = idesc_f16_f32(ATT_BM, ATT_BN, false, false);
+// S-shaped MMA of one unit (M = 128, N = 64, K = D): D[tmem] = A_tile *
+// B_rows^T, A a [128 rows][D] tile and B 64 rows of one, both stored as D/64
+// 64-wide 128-byte-swizzled boxes; `b_addr` points at the unit's first row
+// (tile base + 64 * 128 B for the second half).
+template <int D>
+__device__ __forceinline__ void atb_mma_nt_unit(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
+  constexpr uint32_t IDESC = idesc_f16_f32(ATT_BM, ATT_BN / 2, false, false);
 #pragma unroll
-  for (int kk = 0; kk < ATT_D / 16; ++kk) {
+  for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-    umma_f16_ss(d_tmem, sw128_desc(a_addr + off, 16, 1024), sw128_desc(b_addr + off, 16, 1024), IDESC_S,
+    umma_f16_ss(d_tmem, sw128_desc(a_addr + off, 16, 1024), sw128_desc(b_addr + off, 16, 1024), IDESC,
                 kk > 0 ? 1u : 0u);
   }
 }
 
-// PV-shaped MMA (M = 128, N = D, K = 128): D[tmem] (+)= A[tmem, fp16 pairs in
-// 64 columns] * B_tile, B a [128 K rows][128 D] tile read MN-major.
-__device__ __forceinline__ void atb_mma_tn(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, bool acc) {
-  constexpr uint32_t IDESC_O = idesc_f16_f32(ATT_BM, ATT_D, false, true);
+// Accumulating MMA of one unit (M = 128, N = D, K = 64): D[tmem] (+)=
+// A[tmem, fp16 pairs in 32 columns] * B, B the unit's 64 rows of a
+// [rows][D] tile read MN-major (`b_addr` at the unit's first row).
+template <int D>
+__device__ __forceinline__ void atb_mma_tn_unit(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, bool acc) {
+  constexpr uint32_t IDESC = idesc_f16_f32(ATT_BM, D, false, true);
 #pragma unroll
-  for (int kk = 0; kk < ATT_BN / 16; ++kk)
-    umma_f16_ts(d_tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 2048, 16384, 1024), IDESC_O,
+  for (int kk = 0; kk < ATT_BN / 32; ++kk)
+    umma_f16_ts(d_tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 2048, 16384, 1024), IDESC,
                 (acc || kk > 0) ? 1u : 0u);
 }
 
+template <int D>
 __global__ void __launch_bounds__(ATB_THREADS, 1)
     attention_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                               const AttnBwdArgs args) {
+  constexpr int TB = AtbCfg<D>::TILE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sK = smem;
-  uint8_t* sV = sK + ATT_TILE_BYTES;
-  uint8_t* sQ = sV + ATT_TILE_BYTES;                      // [STAGES]
-  uint8_t* sdO = sQ + ATB_STAGES * ATT_TILE_BYTES;        // [STAGES]
-  float* sL = reinterpret_cast<float*>(sdO + ATB_STAGES * ATT_TILE_BYTES);  // [STAGES][128]
+  uint8_t* sV = sK + TB;
+  uint8_t* sQ = sV + TB;                      // [STAGES]
+  uint8_t* sdO = sQ + ATB_STAGES * TB;        // [STAGES]
+  float* sL = reinterpret_cast<float*>(sdO + ATB_STAGES * TB);  // [STAGES][128]
   float* sD = sL + ATB_STAGES * ATT_BM;                                      // [STAGES][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sD + ATB_STAGES * ATT_BM);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;                 // STAGES
   uint64_t* q_empty = q_full + ATB_STAGES;     // STAGES
-  uint64_t* s_full = q_empty + ATB_STAGES;     // S^T, dP^T in TMEM
-  uint64_t* p_full = s_full + 1;               // P^T, dS^T in TMEM
-  uint64_t* acc_full = p_full + 1;             // dK, dV complete
+  uint64_t* s_full = q_empty + ATB_STAGES;     // 2: a unit's S^T, dP^T in buffer b
+  uint64_t* p_full = s_full + 2;               // 2: its P^T, dS^T in buffer b
+  uint64_t* buf_free = p_full + 2;             // 2: the MMAs reading buffer b's P^T, dS^T completed
+  uint64_t* acc_full = buf_free + 2;           // dK, dV complete
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -215,7 +244,8 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   const int kv0 = blockIdx.x * ATT_BN;
   const int group = args.heads_q / args.heads_kv;
   const int nq = args.R_pad / ATT_BM;
-  const int iters = group * nq;
+  const int iters = group * nq;   // streamed Q / dO tiles
+  const int units = 2 * iters;    // unit u: half u & 1 of tile u >> 1
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -223,8 +253,11 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, ATT_BM);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], ATT_BM);
+      mbar_init(&buf_free[i], 1);
+    }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -245,18 +278,18 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(kv_full, 2 * ATT_TILE_BYTES);
-      att_load_tile(&tmK, kv_full, sK, args.layout, kv0, hk, b);
-      att_load_tile(&tmV, kv_full, sV, args.layout, kv0, hk, b);
+      mbar_arrive_expect_tx(kv_full, 2 * TB);
+      att_load_tile_d<D>(&tmK, kv_full, sK, args.layout, kv0, hk, b);
+      att_load_tile_d<D>(&tmV, kv_full, sV, args.layout, kv0, hk, b);
       int issued = 0;
       for (int n = 0; n < iters; ++n) {
         const int s = n % ATB_STAGES;
         if (!mbar_wait(&q_empty[s], ((n / ATB_STAGES) & 1) ^ 1, wd, SITE_ATB_PRODUCER)) break;
         const int hq = hk * group + n / nq;
         const int i = n % nq;
-        mbar_arrive_expect_tx(&q_full[s], 2 * ATT_TILE_BYTES + 2 * ATB_VEC_BYTES);
-        att_load_tile(&tmQ, &q_full[s], sQ + s * ATT_TILE_BYTES, args.layout, i * ATT_BM, hq, b);
-        att_load_tile(&tmdO, &q_full[s], sdO + s * ATT_TILE_BYTES, args.layout, i * ATT_BM, hq, b);
+        mbar_arrive_expect_tx(&q_full[s], 2 * TB + 2 * ATB_VEC_BYTES);
+        att_load_tile_d<D>(&tmQ, &q_full[s], sQ + s * TB, args.layout, i * ATT_BM, hq, b);
+        att_load_tile_d<D>(&tmdO, &q_full[s], sdO + s * TB, args.layout, i * ATT_BM, hq, b);
         const long long voff = (static_cast<long long>(b) * args.heads_q + hq) * args.R_pad + i * ATT_BM;
         bulk_load(sL + s * ATT_BM, args.lse2 + voff, ATB_VEC_BYTES, &q_full[s]);
         bulk_load(sD + s * ATT_BM, args.dvec + voff, ATB_VEC_BYTES, &q_full[s]);
@@ -269,22 +302,38 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      bool ok = mbar_wait(kv_full, 0, wd, SITE_ATB_MMA_FIXED);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      for (int n = 0; n < iters && ok; ++n) {
-        const int s = n % ATB_STAGES;
-        if (!mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+      // S^T, dP^T of unit u into buffer u & 1 (its Q / dO stage must have landed).
+      auto issue_sdp = [&](int u) -> bool {
+        const int n = u >> 1, hf = u & 1, s = n % ATB_STAGES;
+        if (hf == 0 && !mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + s * ATT_TILE_BYTES);
-        const uint32_t g_addr = smem_u32(sdO + s * ATT_TILE_BYTES);
-        atb_mma_nt(tmem_base + 0, k_addr, q_addr);    // S^T = K_j Q_i^T
-        atb_mma_nt(tmem_base + 128, v_addr, g_addr);  // dP^T = V_j dO_i^T
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, n & 1, wd, SITE_ATB_MMA_P)) break;
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 query rows
+        const uint32_t buf = tmem_base + hf * 128;
+        atb_mma_nt_unit<D>(buf, k_addr, smem_u32(sQ + s * TB) + rows);        // S^T = K_j Q^T
+        atb_mma_nt_unit<D>(buf + 64, v_addr, smem_u32(sdO + s * TB) + rows);  // dP^T = V_j dO^T
+        umma_commit(&s_full[hf]);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, wd, SITE_ATB_MMA_FIXED);
+      if (ok) ok = issue_sdp(0);
+      if (ok && units > 1) ok = issue_sdp(1);
+      for (int u = 0; u < units && ok; ++u) {
+        const int n = u >> 1, hf = u & 1, s = n % ATB_STAGES;
+        const uint32_t par = static_cast<uint32_t>(n & 1);
+        if (!mbar_wait(&p_full[hf], par, wd, SITE_ATB_MMA_P)) break;
         tc_fence_after();
-        atb_mma_tn(tmem_base + 256, tmem_base + 0, g_addr, n > 0);    // dV += P^T dO_i
-        atb_mma_tn(tmem_base + 384, tmem_base + 128, q_addr, n > 0);  // dK += dS^T Q_i
-        umma_commit(&q_empty[s]);
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;
+        const uint32_t buf = tmem_base + hf * 128;
+        atb_mma_tn_unit<D>(tmem_base + 256, buf, smem_u32(sdO + s * TB) + rows, u > 0);      // dV += P^T dO
+        atb_mma_tn_unit<D>(tmem_base + 256 + D, buf + 64, smem_u32(sQ + s * TB) + rows, u > 0);  // dK += dS^T Q
+        umma_commit(&buf_free[hf]);
+        if (hf == 1) umma_commit(&q_empty[s]);
+        if (u + 2 < units) {
+          // Unit u + 2 reuses this buffer: its S^T overwrites the P^T just read.
+          if (!mbar_wait(&buf_free[hf], par, wd, SITE_ATB_MMA_FREE)) break;
+          ok = issue_sdp(u + 2);
+        }
       }
       umma_commit(acc_full);
       umma_commit(drain);
@@ -292,43 +341,41 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ P^T, dS^T and the epilogue
+    const int hf = (warp - 4) >> 2;  // buffer (query half) of this warpgroup
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;  // key row within the tile
+    const int r = qd * 32 + lane;    // key row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t tS = tmem_base + lane_off;
-    const uint32_t tP = tmem_base + 128 + lane_off;
+    const uint32_t tS = tmem_base + hf * 128 + lane_off;
+    const uint32_t tP = tS + 64;
     bool ok = true;
     for (int n = 0; n < iters; ++n) {
       const int s = n % ATB_STAGES;
       // The stage's LSE / D vectors arrive by bulk copy on q_full[s]; waiting
       // on that phase too makes them visible here. It cannot have moved on:
-      // the stage is refilled only after this iteration's p_full.
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, n & 1, wd, SITE_ATB_EW_S) &&
+      // the stage is refilled only after this unit's p_full.
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hf], n & 1, wd, SITE_ATB_EW_S) &&
                                        mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_EW_S));
       if (!ok) break;
       tc_fence_after();
-      const float* L = sL + s * ATT_BM;
-      const float* Dv = sD + s * ATT_BM;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pp[32], pd[32];
-        atb_elementwise_half(
-            tS, tP, half, args.scale_log2, args.scale, [&](int c) { return L[c]; }, [&](int c) { return Dv[c]; },
-            [](int) { return true; }, pp, pd);
-        tmem_st_32x32b_x32(tS + half * 32, pp);
-        tmem_st_32x32b_x32(tP + half * 32, pd);
-      }
+      const float* L = sL + s * ATT_BM + hf * 64;
+      const float* Dv = sD + s * ATT_BM + hf * 64;
+      atb_elementwise_unit(
+          tS, tP, args.scale_log2, args.scale, [&](int c) { return L[c]; }, [&](int c) { return Dv[c]; },
+          [](int) { return true; }, true);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[hf]);
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
       tc_fence_after();
       const int row = kv0 + r;
       const bool live = row < args.C;
-      const long long off = attn_row_offset(args.layout, b, args.heads_kv, args.C, hk, live ? row : 0);
-      atb_store_row(tmem_base + 256 + lane_off, live ? args.dV + off : nullptr);
-      atb_store_row(tmem_base + 384 + lane_off, live ? args.dK + off : nullptr);
+      const long long off = attn_row_offset(args.layout, b, args.heads_kv, args.C, hk, live ? row : 0, D);
+      // warpgroup 0 stores dV, warpgroup 1 dK
+      if (hf == 0)
+        atb_store_row<D>(tmem_base + 256 + lane_off, live ? args.dV + off : nullptr);
+      else
+        atb_store_row<D>(tmem_base + 256 + D + lane_off, live ? args.dK + off : nullptr);
     }
   }
 
@@ -340,24 +387,27 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   }
 }
 
+template <int D>
 __global__ void __launch_bounds__(ATB_THREADS, 1)
     attention_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                             const AttnBwdArgs args) {
+  constexpr int TB = AtbCfg<D>::TILE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sQ = smem;
-  uint8_t* sdO = sQ + ATT_TILE_BYTES;
-  uint8_t* sK = sdO + ATT_TILE_BYTES;                  // [STAGES]
-  uint8_t* sV = sK + ATB_STAGES * ATT_TILE_BYTES;      // [STAGES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ATB_STAGES * ATT_TILE_BYTES);
+  uint8_t* sdO = sQ + TB;
+  uint8_t* sK = sdO + TB;                  // [STAGES]
+  uint8_t* sV = sK + ATB_STAGES * TB;      // [STAGES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ATB_STAGES * TB);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                // STAGES
   uint64_t* kv_empty = kv_full + ATB_STAGES;   // STAGES
-  uint64_t* s_full = kv_empty + ATB_STAGES;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* acc_full = p_full + 1;
+  uint64_t* s_full = kv_empty + ATB_STAGES;    // 2
+  uint64_t* p_full = s_full + 2;               // 2
+  uint64_t* buf_free = p_full + 2;             // 2
+  uint64_t* acc_full = buf_free + 2;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -369,6 +419,7 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   const int q0 = blockIdx.x * ATT_BM;
   const int hk = h / (args.heads_q / args.heads_kv);
   const int nkv = (args.C + ATT_BN - 1) / ATT_BN;
+  const int units = 2 * nkv;  // unit u: key half u & 1 of tile u >> 1
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -376,8 +427,11 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, ATT_BM);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], ATT_BM);
+      mbar_init(&buf_free[i], 1);
+    }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -398,16 +452,16 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(q_full, 2 * ATT_TILE_BYTES);
-      att_load_tile(&tmQ, q_full, sQ, args.layout, q0, h, b);
-      att_load_tile(&tmdO, q_full, sdO, args.layout, q0, h, b);
+      mbar_arrive_expect_tx(q_full, 2 * TB);
+      att_load_tile_d<D>(&tmQ, q_full, sQ, args.layout, q0, h, b);
+      att_load_tile_d<D>(&tmdO, q_full, sdO, args.layout, q0, h, b);
       int issued = 0;
       for (int j = 0; j < nkv; ++j) {
         const int s = j % ATB_STAGES;
         if (!mbar_wait(&kv_empty[s], ((j / ATB_STAGES) & 1) ^ 1, wd, SITE_ATB_PRODUCER)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * ATT_TILE_BYTES);
-        att_load_tile(&tmK, &kv_full[s], sK + s * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
-        att_load_tile(&tmV, &kv_full[s], sV + s * ATT_TILE_BYTES, args.layout, j * ATT_BN, hk, b);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TB);
+        att_load_tile_d<D>(&tmK, &kv_full[s], sK + s * TB, args.layout, j * ATT_BN, hk, b);
+        att_load_tile_d<D>(&tmV, &kv_full[s], sV + s * TB, args.layout, j * ATT_BN, hk, b);
         issued = j + 1;
       }
       mbar_wait(q_full, 0, wd, SITE_ATB_PRODUCER_DRAIN);
@@ -417,21 +471,36 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      bool ok = mbar_wait(q_full, 0, wd, SITE_ATB_MMA_FIXED);
       const uint32_t q_addr = smem_u32(sQ), g_addr = smem_u32(sdO);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j % ATB_STAGES;
-        if (!mbar_wait(&kv_full[s], (j / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+      // S, dP of unit u (keys of half u & 1 of tile u >> 1) into buffer u & 1.
+      auto issue_sdp = [&](int u) -> bool {
+        const int j = u >> 1, hf = u & 1, s = j % ATB_STAGES;
+        if (hf == 0 && !mbar_wait(&kv_full[s], (j / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * ATT_TILE_BYTES);
-        const uint32_t v_addr = smem_u32(sV + s * ATT_TILE_BYTES);
-        atb_mma_nt(tmem_base + 0, q_addr, k_addr);    // S = Q_i K_j^T
-        atb_mma_nt(tmem_base + 128, g_addr, v_addr);  // dP = dO_i V_j^T
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1, wd, SITE_ATB_MMA_P)) break;
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 key rows
+        const uint32_t buf = tmem_base + hf * 128;
+        atb_mma_nt_unit<D>(buf, q_addr, smem_u32(sK + s * TB) + rows);       // S = Q_i K^T
+        atb_mma_nt_unit<D>(buf + 64, g_addr, smem_u32(sV + s * TB) + rows);  // dP = dO_i V^T
+        umma_commit(&s_full[hf]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, wd, SITE_ATB_MMA_FIXED);
+      if (ok) ok = issue_sdp(0);
+      if (ok && units > 1) ok = issue_sdp(1);
+      for (int u = 0; u < units && ok; ++u) {
+        const int j = u >> 1, hf = u & 1, s = j % ATB_STAGES;
+        const uint32_t par = static_cast<uint32_t>(j & 1);
+        if (!mbar_wait(&p_full[hf], par, wd, SITE_ATB_MMA_P)) break;
         tc_fence_after();
-        atb_mma_tn(tmem_base + 256, tmem_base + 0, k_addr, j > 0);  // dQ += dS K_j
-        umma_commit(&kv_empty[s]);
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;
+        atb_mma_tn_unit<D>(tmem_base + 256, tmem_base + hf * 128, smem_u32(sK + s * TB) + rows,
+                        u > 0);  // dQ += dS K
+        umma_commit(&buf_free[hf]);
+        if (hf == 1) umma_commit(&kv_empty[s]);
+        if (u + 2 < units) {
+          if (!mbar_wait(&buf_free[hf], par, wd, SITE_ATB_MMA_FREE)) break;
+          ok = issue_sdp(u + 2);
+        }
       }
       umma_commit(acc_full);
       umma_commit(drain);
@@ -439,38 +508,35 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dS and the epilogue
+    const int hf = (warp - 4) >> 2;  // buffer (key half) of this warpgroup
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;  // query row within the tile
+    const int r = qd * 32 + lane;    // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t tS = tmem_base + lane_off;
-    const uint32_t tP = tmem_base + 128 + lane_off;
+    const uint32_t tS = tmem_base + hf * 128 + lane_off;
+    const uint32_t tP = tS + 64;
     const long long voff = (static_cast<long long>(b) * args.heads_q + h) * args.R_pad + q0 + r;
     const float lse2 = args.lse2[voff];
     const float dterm = args.dvec[voff];
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, wd, SITE_ATB_EW_S));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hf], j & 1, wd, SITE_ATB_EW_S));
       if (!ok) break;
       tc_fence_after();
-      const int valid = args.C - j * ATT_BN;  // key columns of this tile inside C
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pp[32], pd[32];
-        atb_elementwise_half(
-            tS, tP, half, args.scale_log2, args.scale, [&](int) { return lse2; }, [&](int) { return dterm; },
-            [&](int c) { return c < valid; }, pp, pd);
-        tmem_st_32x32b_x32(tS + half * 32, pd);  // dS over S; P is not needed here
-      }
+      const int valid = args.C - j * ATT_BN - hf * 64;  // key columns of this unit inside C
+      // dS over S (the MMA reads dS from the S columns); P is not needed here.
+      atb_elementwise_unit(
+          tS, tP, args.scale_log2, args.scale, [&](int) { return lse2; }, [&](int) { return dterm; },
+          [&](int c) { return c < valid; }, false);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[hf]);
     }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
+    if (ok && hf == 0 && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
       tc_fence_after();
       const int row = q0 + r;
       const bool live = row < args.R;
-      const long long off = attn_row_offset(args.layout, b, args.heads_q, args.R, h, live ? row : 0);
-      atb_store_row(tmem_base + 256 + lane_off, live ? args.dQ + off : nullptr);
+      const long long off = attn_row_offset(args.layout, b, args.heads_q, args.R, h, live ? row : 0, D);
+      atb_store_row<D>(tmem_base + 256 + lane_off, live ? args.dQ + off : nullptr);
     }
   }
 

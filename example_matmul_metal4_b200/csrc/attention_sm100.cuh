@@ -111,19 +111,6 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 #define ATT_EMU_PER8 2
 #endif
 
-// Loads one 128-row x 128-D tile as two 64-wide boxes (D 0..63, 64..127);
-// the backward kernels' loader.
-__device__ __forceinline__ void att_load_tile(const CUtensorMap* map, uint64_t* bar, uint8_t* dst, int layout,
-                                              int row0, int head, int b) {
-  if (layout == 0) {  // dims {D, S, H, B}
-    tma_load_4d(map, bar, dst, 0, row0, head, b);
-    tma_load_4d(map, bar, dst + 16384, 64, row0, head, b);
-  } else {  // dims {D, H, S, B}
-    tma_load_4d(map, bar, dst, 0, head, row0, b);
-    tma_load_4d(map, bar, dst + 16384, 64, head, row0, b);
-  }
-}
-
 // Per-head-dim constants of the forward kernel. A tile is 128 rows x D
 // fp16, loaded as D/64 boxes of 64 columns (128-byte swizzle); TMEM holds
 // S0 | S1 (128 columns each) then O0 | O1 (D columns each).

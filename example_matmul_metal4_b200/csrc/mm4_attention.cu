@@ -141,6 +141,37 @@ mm4_status attention_forward(const mm4_attention_plan* p, const void* Q, const v
   return launch_forward<64>(tq, tk, tv, args, d, st, duplicated_count);
 }
 
+template <int D>
+mm4_status launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
+                           const AttnBwdArgs& args, const mm4_attention_desc& d, const void* O, const void* dO,
+                           const float* lse, cudaStream_t st, int sm_count) {
+  const long long rows_total = static_cast<long long>(d.batch) * d.heads_q * args.R_pad;
+  const int prep_grid = static_cast<int>(std::min<long long>((rows_total + 7) / 8, 16ll * sm_count));
+  attention_bwd_prep_kernel<D><<<prep_grid, 256, 0, st>>>(static_cast<const __half*>(O),
+                                                           static_cast<const __half*>(dO), lse,
+                                                           const_cast<float*>(args.lse2), const_cast<float*>(args.dvec),
+                                                           d.batch, d.heads_q, d.rows, args.R_pad, d.layout);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_prep_kernel launch");
+
+  dim3 grid_kv((d.columns + ATT_BN - 1) / ATT_BN, d.heads_kv, d.batch);
+  dim3 grid_q(args.R_pad / ATT_BM, d.heads_q, d.batch);
+  if (grid_kv.y > 65535 || grid_kv.z > 65535 || grid_q.y > 65535)
+    return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
+  constexpr int dkdv_smem = AtbCfg<D>::DKDV_SMEM;
+  constexpr int dq_smem = AtbCfg<D>::DQ_SMEM;
+  mm4_status rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dkdv_kernel<D>), dkdv_smem);
+  if (rc == MM4_OK) rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dq_kernel<D>), dq_smem);
+  if (rc != MM4_OK) return rc;
+  attention_bwd_dkdv_kernel<D><<<grid_kv, ATB_THREADS, dkdv_smem, st>>>(tq, tk, tv, tdo, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dkdv_kernel launch");
+  attention_bwd_dq_kernel<D><<<grid_q, ATB_THREADS, dq_smem, st>>>(tq, tk, tv, tdo, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dq_kernel launch");
+  return MM4_OK;
+}
+
 int padded_rows(const mm4_attention_desc& d) { return (d.rows + ATT_BM - 1) / ATT_BM * ATT_BM; }
 
 size_t bwd_workspace_bytes(const mm4_attention_desc& d) {
@@ -168,9 +199,6 @@ mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const v
                              const void* dO, const float* lse, void* dQ, void* dK, void* dV, void* workspace,
                              size_t workspace_bytes, mm4_stream_t stream) {
   if (!p) return fail(MM4_ERR_INVALID, "null plan");
-  if (p->d.head_dim != ATT_D)
-    return fail(MM4_ERR_UNSUPPORTED, "attention backward: head_dim %d (this build's backward implements 128)",
-                p->d.head_dim);
   if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV)
     return fail(MM4_ERR_INVALID, "null tensor pointer");
   const void* ptrs[] = {Q, K, V, O, dO, dQ, dK, dV};
@@ -216,27 +244,8 @@ mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const v
   args.timeout_ns = wait_timeout_ns();
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const long long rows_total = static_cast<long long>(d.batch) * d.heads_q * R_pad;
-  const int prep_grid = static_cast<int>(std::min<long long>((rows_total + 7) / 8, 16ll * info.sm_count));
-  attention_bwd_prep_kernel<<<prep_grid, 256, 0, st>>>(static_cast<const __half*>(O), static_cast<const __half*>(dO),
-                                                        lse, lse2, dvec, d.batch, d.heads_q, d.rows, R_pad, d.layout);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_prep_kernel launch");
-
-  dim3 grid_kv((d.columns + ATT_BN - 1) / ATT_BN, d.heads_kv, d.batch);
-  dim3 grid_q(R_pad / ATT_BM, d.heads_q, d.batch);
-  if (grid_kv.y > 65535 || grid_kv.z > 65535 || grid_q.y > 65535)
-    return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
-  rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dkdv_kernel), ATB_DKDV_SMEM);
-  if (rc == MM4_OK) rc = ensure_smem_attr(reinterpret_cast<const void*>(attention_bwd_dq_kernel), ATB_DQ_SMEM);
-  if (rc != MM4_OK) return rc;
-  attention_bwd_dkdv_kernel<<<grid_kv, ATB_THREADS, ATB_DKDV_SMEM, st>>>(tq, tk, tv, tdo, args);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dkdv_kernel launch");
-  attention_bwd_dq_kernel<<<grid_q, ATB_THREADS, ATB_DQ_SMEM, st>>>(tq, tk, tv, tdo, args);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "attention_bwd_dq_kernel launch");
-  return MM4_OK;
+  if (d.head_dim == 128) return launch_backward<128>(tq, tk, tv, tdo, args, d, O, dO, lse, st, info.sm_count);
+  return launch_backward<64>(tq, tk, tv, tdo, args, d, O, dO, lse, st, info.sm_count);
 }
 
 }  // extern "C"

@@ -40,11 +40,12 @@ def gemm_cases():
 
 def attention_cases():
     out = {}
-    for name, (B, Hq, Hk, R, C, layout, seed) in {
-        "bhsd_1x2_r37_c45": (1, 2, 2, 37, 45, 0, 201),
-        "bshd_2x2_gqa_r20_c33": (2, 2, 1, 20, 33, 1, 202),
+    for name, (B, Hq, Hk, R, C, layout, seed, D) in {
+        "bhsd_1x2_r37_c45": (1, 2, 2, 37, 45, 0, 201, 128),
+        "bshd_2x2_gqa_r20_c33": (2, 2, 1, 20, 33, 1, 202, 128),
+        "bhsd_1x2_r37_c45_d64": (1, 2, 2, 37, 45, 0, 203, 64),
+        "bshd_2x2_gqa_r20_c33_d64": (2, 2, 1, 20, 33, 1, 204, 64),
     }.items():
-        D = 128
         qs = (B, Hq, R, D) if layout == 0 else (B, R, Hq, D)
         ks = (B, Hk, C, D) if layout == 0 else (B, C, Hk, D)
         Q = data.normal(qs, 1.0, seed, 0)
@@ -52,18 +53,19 @@ def attention_cases():
         V = data.normal(ks, 1.0, seed, 2)
         ref = oracle.attention(Q, K, V, B, Hq, Hk, R, C, D, 1 / np.sqrt(D), layout)
         out.update({f"{name}/Q": Q, f"{name}/K": K, f"{name}/V": V, f"{name}/out": ref,
-                    f"{name}/dims": np.array([B, Hq, Hk, R, C, layout])})
+                    f"{name}/dims": np.array([B, Hq, Hk, R, C, layout, D])})
     return out
 
 
 def attention_bwd_cases():
     """dQ, dK, dV and the row LSE of the loss sum(dO * O) (Network.swift:181-401 restated)."""
     out = {}
-    for name, (B, Hq, Hk, R, C, layout, seed) in {
-        "bhsd_1x2_r19_c23": (1, 2, 2, 19, 23, 0, 301),
-        "bshd_1x4_gqa_r12_c17": (1, 4, 2, 12, 17, 1, 302),
+    for name, (B, Hq, Hk, R, C, layout, seed, D) in {
+        "bhsd_1x2_r19_c23": (1, 2, 2, 19, 23, 0, 301, 128),
+        "bshd_1x4_gqa_r12_c17": (1, 4, 2, 12, 17, 1, 302, 128),
+        "bhsd_1x2_r19_c23_d64": (1, 2, 2, 19, 23, 0, 303, 64),
+        "bshd_1x4_gqa_r12_c17_d64": (1, 4, 2, 12, 17, 1, 304, 64),
     }.items():
-        D = 128
         qs = (B, Hq, R, D) if layout == 0 else (B, R, Hq, D)
         ks = (B, Hk, C, D) if layout == 0 else (B, C, Hk, D)
         Q = data.normal(qs, 1.0, seed, 0)
@@ -73,7 +75,7 @@ def attention_bwd_cases():
         dQ, dK, dV, lse = oracle.attention_bwd(Q, K, V, dO, B, Hq, Hk, R, C, D, 1 / np.sqrt(D), layout)
         out.update({f"{name}/Q": Q, f"{name}/K": K, f"{name}/V": V, f"{name}/dO": dO, f"{name}/dQ": dQ,
                     f"{name}/dK": dK, f"{name}/dV": dV, f"{name}/lse": lse,
-                    f"{name}/dims": np.array([B, Hq, Hk, R, C, layout])})
+                    f"{name}/dims": np.array([B, Hq, Hk, R, C, layout, D])})
     return out
 
 

@@ -38,8 +38,8 @@ def test_gemm_fixtures(cuda):
 def test_attention_forward_fixtures(cuda):
     z, names = _cases("attention_small.npz")
     for n in names:
-        B, Hq, Hk, R, C, layout = (int(v) for v in z[f"{n}/dims"])
-        plan = AttentionPlan(AttentionDimensions(R, C, 128, Hq, Hk), batch=B, layout=layout)
+        B, Hq, Hk, R, C, layout, D = (int(v) for v in z[f"{n}/dims"])
+        plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
         O = plan.run(_t(z[f"{n}/Q"], cuda), _t(z[f"{n}/K"], cuda), _t(z[f"{n}/V"], cuda))
         sync_check()
         got = O.float().cpu().numpy()
@@ -54,8 +54,8 @@ def test_attention_backward_fixtures(cuda):
     import torch
     z, names = _cases("attention_bwd_small.npz")
     for n in names:
-        B, Hq, Hk, R, C, layout = (int(v) for v in z[f"{n}/dims"])
-        plan = AttentionPlan(AttentionDimensions(R, C, 128, Hq, Hk), batch=B, layout=layout)
+        B, Hq, Hk, R, C, layout, D = (int(v) for v in z[f"{n}/dims"])
+        plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
         tQ, tK, tV, tdO = (_t(z[f"{n}/{k}"], cuda) for k in ("Q", "K", "V", "dO"))
         lse = torch.empty(plan.lse_shape(), dtype=torch.float32, device=cuda)
         O = plan.run(tQ, tK, tV, lse=lse)

@@ -295,8 +295,8 @@ def test_golden_attention_fixtures():
     z = np.load(GOLDEN / "attention_small.npz")
     names = sorted({k.split("/")[0] for k in z.files})
     for n in names:
-        B, Hq, Hk, R, C, layout = (int(v) for v in z[f"{n}/dims"])
-        got = oracle.attention(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], B, Hq, Hk, R, C, 128, 1 / np.sqrt(128),
+        B, Hq, Hk, R, C, layout, D = (int(v) for v in z[f"{n}/dims"])
+        got = oracle.attention(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], B, Hq, Hk, R, C, D, 1 / np.sqrt(D),
                                layout)
         np.testing.assert_allclose(got, z[f"{n}/out"], rtol=1e-6, atol=1e-7)
 
@@ -306,10 +306,10 @@ def test_golden_attention_backward_fixtures():
     above is the mathematical one)."""
     z = np.load(GOLDEN / "attention_bwd_small.npz")
     names = sorted({k.split("/")[0] for k in z.files})
-    assert len(names) == 2
+    assert len(names) == 4
     for n in names:
-        B, Hq, Hk, R, C, layout = (int(v) for v in z[f"{n}/dims"])
-        got = oracle.attention_bwd(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], z[f"{n}/dO"], B, Hq, Hk, R, C, 128,
-                                   1 / np.sqrt(128), layout)
+        B, Hq, Hk, R, C, layout, D = (int(v) for v in z[f"{n}/dims"])
+        got = oracle.attention_bwd(z[f"{n}/Q"], z[f"{n}/K"], z[f"{n}/V"], z[f"{n}/dO"], B, Hq, Hk, R, C, D,
+                                   1 / np.sqrt(D), layout)
         for i, key in enumerate(("dQ", "dK", "dV", "lse")):
             np.testing.assert_allclose(got[i], z[f"{n}/{key}"], rtol=1e-6, atol=1e-7, err_msg=f"{n} {key}")
