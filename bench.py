@@ -388,7 +388,7 @@ def burn(step, flush, seconds, dist):
 
 # ---------------------------------------------------------------------------
 # mm4 arm: per-workload step builders
-# Each returns (step, e2e_step, (h2d, d2h) bytes, kernel name, launches/step, scaling).
+# Each returns (step, e2e_step, (h2d, d2h) bytes, kernel name, launches/step, scaling, input sets).
 # ---------------------------------------------------------------------------
 
 L2_BYTES = 126 * 1000 * 1000  # B200 L2
@@ -406,6 +406,14 @@ def input_sets(first, l2):
     nbytes = sum(t.numel() * t.element_size() for t in first.values())
     n = max(2, 1 + math.ceil(2 * L2_BYTES / nbytes))
     return [first] + [{k: v.clone() for k, v in first.items()} for _ in range(n - 1)]
+
+
+def check_rotation(w, dist, sets):
+    """The config line states rotated_input_bytes(); fail loudly if a builder rotates something else."""
+    got = sum(t.numel() * t.element_size() for t in sets[0].values())
+    want = rotated_input_bytes(w, dist.world, dist.rank)
+    if got != want:
+        raise SystemExit(f"rotated inputs are {got} bytes, rotated_input_bytes() says {want}")
 
 
 def cycling(sets):
@@ -470,7 +478,7 @@ def build_gemm(w, dist, dev, gen, l2):
                 hC.copy_(grp.C, non_blocking=True)
         e2e_bytes = (A.numel() * 2 + B.numel() * 2, M * N * 2 if r == 0 else 0)
         return (step, e2e_step, e2e_bytes, plan.kernel_name + " + in-kernel cross-GPU reduce over peer memory", 1,
-                "strong", len(sets))
+                "strong", sets)
     n0, Nr = shard_range(N, P, r, align=8)  # column blocks of whole 16-byte groups
     t = w.inputs(dev, gen, N=Nr)
     A, B, bias = t["A"], t["B"], t["bias"]
@@ -509,7 +517,7 @@ def build_gemm(w, dist, dev, gen, l2):
         plan.run(A, B, bias, C=C, workspace=ws)
         hC.copy_(C, non_blocking=True)
     e2e_bytes = (A.numel() * 2 + B.numel() * 2 + bias.numel() * 2, C.numel() * 2)
-    return step, e2e_step, e2e_bytes, plan.kernel_name, 1, "strong", len(sets)
+    return step, e2e_step, e2e_bytes, plan.kernel_name, 1, "strong", sets
 
 
 def _attention_shard(w, dist):
@@ -556,7 +564,7 @@ def build_attention(w, dist, dev, gen, l2):
         V.copy_(hV, non_blocking=True)
         plan.run(Q, K, V, O=O)
         hO.copy_(O, non_blocking=True)
-    return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "strong", len(sets)
+    return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "strong", sets
 
 
 def build_attention_bwd(w, dist, dev, gen, l2):
@@ -600,7 +608,7 @@ def build_attention_bwd(w, dist, dev, gen, l2):
     h2d = sum(v.numel() * v.element_size() for v in sets[0].values())
     d2h = 3 * Q.numel() * 2
     return (step, e2e_step, (h2d, d2h), "attention_bwd_sm100 (prep + dK/dV + dQ kernels)", 3, "strong",
-            len(sets))
+            sets)
 
 
 def build_conv(w, dist, dev, gen, l2):
@@ -653,7 +661,7 @@ def build_conv(w, dist, dev, gen, l2):
         plan.run(x, wt, bias, y=y)
         hy.copy_(y, non_blocking=True)
     return (step, e2e_step, ((x.numel() + wt.numel() + bias.numel()) * 2, y.numel() * 2), plan.kernel_name, 1,
-            "strong", len(sets))
+            "strong", sets)
 
 
 def run_mm4(args, w, dist, peaks):
@@ -668,7 +676,10 @@ def run_mm4(args, w, dist, peaks):
     builder = (build_gemm if isinstance(w, GemmWorkload) else
                build_attention_bwd if isinstance(w, AttentionBwdWorkload) else
                build_attention if isinstance(w, AttentionWorkload) else build_conv)
-    step, e2e_step, e2e_bytes, kernel_name, launches, scaling, nsets = builder(w, dist, dev, gen, args.l2)
+    step, e2e_step, e2e_bytes, kernel_name, launches, scaling, sets = builder(w, dist, dev, gen, args.l2)
+    nsets = len(sets)
+    if args.l2 == "rotate":
+        check_rotation(w, dist, sets)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if args.l2 == "flush" else None
 
     step()
@@ -842,6 +853,42 @@ def cpu_sample(w, seconds_hint=10.0, threads=None):
 # main
 # ---------------------------------------------------------------------------
 
+def parallelism(w, n):
+    """How N GPUs split the named shape (the same text on both arms)."""
+    if n == 1:
+        return "single GPU"
+    if isinstance(w, GemmWorkload) and w.split > 1:
+        return (f"{n} K shards of K = {w.K} on 64-element boundaries, split-K {w.split} within each shard; fp32 "
+                "partials summed inside the split-K kernels over peer memory (NVLink) into rank 0's C; one launch "
+                "per GPU per step")
+    axis = ("(batch, head) units" if isinstance(w, AttentionWorkload) else
+            "C column blocks (A replicated)" if isinstance(w, GemmWorkload) else "batch")
+    return f"{n} shards of one named shape along {axis}, no collective"
+
+
+def rotated_input_bytes(w, n, rank=0):
+    """Bytes of the device inputs a step of rank `rank` reads and rotation copies (see the builders)."""
+    if isinstance(w, GemmWorkload):
+        if n > 1 and w.split > 1:
+            k = shard_range(w.K, n, rank, align=64)[1]
+            return 2 * (w.M * k + k * w.N)
+        cols = shard_range(w.N, n, rank, align=8)[1]
+        return 2 * (w.M * w.K + w.K * cols)
+    if isinstance(w, AttentionWorkload):
+        nb, nh = w.shard(n, rank)
+        per = nb * nh * w.S * w.D * 2
+        if isinstance(w, AttentionBwdWorkload):
+            return 5 * per + nb * nh * w.S * 4  # Q, K, V, O, dO and the fp32 LSE
+        return 3 * per
+    nb = shard_range(w.N, n, rank)[1]
+    return 2 * (nb * w.D * w.H * w.W * w.C + w.O * w.taps() * w.C)
+
+
+def rotate_copies(w, n):
+    """Device copies of rank 0's inputs that input_sets() makes when rotating (the same rule)."""
+    return max(2, 1 + math.ceil(2 * L2_BYTES / rotated_input_bytes(w, n)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -868,11 +915,14 @@ def main():
     base = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "vs_baseline": None, "dtype": "fp16 (fp32 accumulate)",
             "data": "synthetic (seeded torch generator; BASELINE shapes and distributions)"}
+    # The workload's configuration, identical on both arms (the reference arm runs the same named shape on
+    # the host, where the L2 handling does not apply).
     cfg = dict(w.config(), l2="flushed between steps (512 MiB write outside the timed events)",
-               baseline_config_index=w.config_index)
+               baseline_config_index=w.config_index, parallelism=parallelism(w, args.gpus))
     if args.l2 == "rotate":
-        cfg["l2"] = ("inputs larger than L2: each step reads the next of {n} device copies of its inputs, so "
-                     "at least 2 x 126 MB of other inputs pass through L2 between two uses of a copy; no flush")
+        cfg["l2"] = (f"inputs larger than L2: each step reads the next of {rotate_copies(w, args.gpus)} device "
+                     "copies of its inputs, so at least 2 x 126 MB of other inputs pass through L2 between two "
+                     "uses of a copy; no flush")
 
     if args.impl == "reference":
         if dist.rank != 0:
@@ -885,7 +935,7 @@ def main():
                 vals.append(cb["value"])
         value = statistics.mean(vals)
         line = dict(base, impl="reference", value=value, ms_per_step=w.flops() / (value * 1e12) * 1e3,
-                    scaling="strong", config=dict(cfg, l2="n/a (host CPU)"),
+                    scaling="strong", config=cfg, kernel="C restatement of the reference's CPU loops (host)",
                     cpu_baseline={"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
                                   "sample": cb["sample"]},
                     e2e={"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -901,21 +951,8 @@ def main():
             # The reference's own CPU check runs single-threaded; time that too on a smaller sample.
             one = cpu_sample(w, seconds_hint=max(1.0, args.cpu_seconds / 4), threads=1)
             cpu["single_thread"] = {"value": one["value"], "unit": one["unit"], "cores": 1, "sample": one["sample"]}
-        cfg["kernel"] = res["kernel"]
-        cfg["l2"] = cfg["l2"].replace("{n}", str(res["nsets"]))
-        if args.gpus == 1:
-            cfg["parallelism"] = "single GPU"
-        elif isinstance(w, GemmWorkload) and w.split > 1:
-            cfg["parallelism"] = (f"{args.gpus} K shards of K = {w.K} on 64-element boundaries (rank 0: "
-                                  f"{res['shard']}), split-K {w.split} within each shard; fp32 partials summed "
-                                  "inside the split-K kernels over peer memory (NVLink) into rank 0's C; one "
-                                  "launch per GPU per step")
-        else:
-            axis = ("(batch, head) units" if isinstance(w, AttentionWorkload) else
-                    "C column blocks (A replicated)" if isinstance(w, GemmWorkload) else "batch")
-            cfg["parallelism"] = (f"{args.gpus} shards of one named shape along {axis} (rank 0: {res['shard']}), "
-                                  "no collective")
         line = dict(base, value=res["value"], ms_per_step=res["ms"], scaling=res["scaling"], config=cfg,
+                    kernel=res["kernel"], shard_of_rank0=res["shard"],
                     pct_of_measured_bf16_peak=res["value"] / args.gpus / peaks["bf16_tflops"],
                     clocks=res["clocks"], e2e=res["e2e"], roofline=res["roofline"], cpu_baseline=cpu,
                     gpu_launches=res["launches"], launch_only=res["launch_only"], comparator=res["comparator"])

@@ -61,6 +61,11 @@ struct AttnBwdArgs {
 
 constexpr int ATB_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4-7 / 8-11 element-wise (buffer 0 / 1)
 constexpr int ATB_STAGES = 2;
+// Of every 8 exponentials of the element-wise step, this many (an even
+// number) take the FMA-pipe cubic ex2_poly2 and the rest MUFU.
+#ifndef ATB_EMU_PER8
+#define ATB_EMU_PER8 2
+#endif
 constexpr int ATB_VEC_BYTES = ATT_BM * 4;  // one tile's LSE or D values
 template <int D>
 struct AtbCfg {
@@ -140,17 +145,29 @@ __device__ __forceinline__ void atb_elementwise_unit(uint32_t tS, uint32_t tP, f
     tmem_ld_32x32b_x32(tP + c0, vp);
     tmem_ld_wait();
     uint32_t pp[16], pd[16];
+    const float2 sc = make_float2(sl2, sl2);
+    const float2 ds = make_float2(scale, scale);
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int c = c0 + 2 * e;
-      float p0 = ex2_approx(__uint_as_float(vs[2 * e]) * sl2 - lse2_of(c));
-      float p1 = ex2_approx(__uint_as_float(vs[2 * e + 1]) * sl2 - lse2_of(c + 1));
-      if (!valid(c)) p0 = 0.f;
-      if (!valid(c + 1)) p1 = 0.f;
-      const float d0 = p0 * (__uint_as_float(vp[2 * e]) - d_of(c)) * scale;
-      const float d1 = p1 * (__uint_as_float(vp[2 * e + 1]) - d_of(c + 1)) * scale;
-      pp[e] = pack_half2(p0, p1);
-      pd[e] = pack_half2(d0, d1);
+      // exponent pair in one packed FMA; ATB_EMU_PER8 of every 8 exponentials on the FMA pipe
+      const float2 a = ffma2(make_float2(__uint_as_float(vs[2 * e]), __uint_as_float(vs[2 * e + 1])), sc,
+                             make_float2(-lse2_of(c), -lse2_of(c + 1)));
+      float2 pv;
+      if ((e & 3) * 2 >= 8 - ATB_EMU_PER8) {
+        pv = ex2_poly2(a);
+      } else {
+        pv.x = ex2_approx(a.x);
+        pv.y = ex2_approx(a.y);
+      }
+      if (!valid(c)) pv.x = 0.f;
+      if (!valid(c + 1)) pv.y = 0.f;
+      // dS = P * (dP - D) * scale = P * (dP * scale - D * scale)
+      const float2 t = ffma2(make_float2(__uint_as_float(vp[2 * e]), __uint_as_float(vp[2 * e + 1])), ds,
+                             make_float2(-d_of(c) * scale, -d_of(c + 1) * scale));
+      const float2 dv = ffma2(pv, t, make_float2(0.f, 0.f));
+      pp[e] = pack_half2(pv.x, pv.y);
+      pd[e] = pack_half2(dv.x, dv.y);
     }
     if (want_p) {
       tmem_st_32x32b_x16(tS + sub * 16, pp);

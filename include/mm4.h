@@ -233,7 +233,9 @@ MM4_API mm4_status mm4_gemm_splitk_run_distributed(const mm4_gemm_plan* plan, mm
  * `attention` kernel generator and run(...) (Sources/attention/
  * attention.swift:4-21, :23-382, :398-541). Non-causal softmax(Q K^T *
  * scale) V with an fp32 online softmax; O is fp16.
- *  rows = R (query length), columns = C (key/value length), head_dim = D.
+ *  rows = R (query length), columns = C (key/value length), head_dim = D:
+ *  128 (the reference's) or 64 (run(...) takes it as a parameter,
+ *  attention.swift:398); other values return MM4_ERR_UNSUPPORTED.
  *  layout MM4_ATTN_BHSD: tensors [batch][heads][seq][D] (BASELINE);
  *         MM4_ATTN_BSHD: tensors [batch][seq][heads][D] (the reference's
  *         [S][H][D] packing, attention.swift:463-471, with batch outermost).
