@@ -64,7 +64,7 @@ constexpr int ATB_STAGES = 2;
 // Of every 8 exponentials of the element-wise step, this many (an even
 // number) take the FMA-pipe cubic ex2_poly2 and the rest MUFU.
 #ifndef ATB_EMU_PER8
-#define ATB_EMU_PER8 2
+#define ATB_EMU_PER8 0
 #endif
 constexpr int ATB_VEC_BYTES = ATT_BM * 4;  // one tile's LSE or D values
 template <int D>
