@@ -688,9 +688,9 @@ def run_mm4(args, w, dist, peaks):
 
     clocks = ClockSampler(dist.local_rank)
     clocks.start()
-    burn(step, flush, 0.6, dist)
+    burn(step, flush, args.burn_seconds, dist)
     per_step = time_steps(step, args.steps, args.warmup, flush, stream, dist)
-    burn(step, flush, 0.3, dist)
+    burn(step, flush, args.burn_seconds / 2, dist)
     clk = clocks.stop()
     sync_check()
     ms = dist.max(sum(per_step) / len(per_step))
@@ -736,9 +736,9 @@ def run_mm4(args, w, dist, peaks):
         # its own clock record (a long dense run settles at power-capped clocks; a cold one boosts).
         cmp_clocks = ClockSampler(dist.local_rank)
         cmp_clocks.start()
-        burn(torch_step, flush, 0.6, dist)
+        burn(torch_step, flush, args.burn_seconds, dist)
         cmp_ms = sum(time_steps(torch_step, args.steps, args.warmup, flush, stream, dist)) / args.steps
-        burn(torch_step, flush, 0.3, dist)
+        burn(torch_step, flush, args.burn_seconds / 2, dist)
         cmp_clk = cmp_clocks.stop()
         step()
         torch_step()  # every input copy holds the same values, so both outputs are comparable
@@ -899,6 +899,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparator", action="store_true", help="skip the torch (cuBLAS/SDPA/cuDNN) comparator")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--burn-seconds", type=float, default=0.6,
+                    help="untimed repetitions of the step before (and half as long after) the timed steps, so they "
+                         "run at the clocks a sustained run settles at; small values keep profiler captures short")
     ap.add_argument("--l2", default="auto", choices=["auto", "rotate", "flush"],
                     help="keep inputs out of L2 by rotating device copies of them or by a 512 MiB write between "
                          "steps; auto: rotate for HBM-bound and small workloads (a write flush leaves ~126 MB of "
