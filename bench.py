@@ -427,6 +427,17 @@ def cycling(sets):
     return nxt
 
 
+def shard_splits(w, n):
+    """Split-K count within each K shard: the named shape's split, reduced so that every split still covers
+    at least SPLIT_MIN_K of the shard (each split reduces a full fp32 M x N partial, so thin splits cost more
+    reduction traffic than they save main-loop time): 32 on 1-4 GPUs at K = 65536, 16 on 8."""
+    k = shard_range(w.K, n, 0, align=64)[1]
+    return max(1, min(w.split, k // SPLIT_MIN_K))
+
+
+SPLIT_MIN_K = 512
+
+
 def _same_on_every_rank(value, what):
     """Raises unless every rank passes the same `value` (plans whose tiles must agree across ranks)."""
     import torch.distributed as tdist
@@ -455,7 +466,7 @@ def build_gemm(w, dist, dev, gen, l2):
         bias = t["bias"]
         tdist.broadcast(bias, src=0)  # one bias for the whole problem
         plan = GemmPlan(GEMMDimensions(M, N, Kr), transpose=(False, False), bias=True,
-                        buildOptions=BuildOptions(splitK=w.split))
+                        buildOptions=BuildOptions(splitK=shard_splits(w, P)))
         _same_on_every_rank((plan.kernel_name, plan.workspace_bytes), "split-K group plan")
         grp = SplitKGroup(plan, root=0)
         sets = input_sets({"A": A, "B": B}, l2)
@@ -858,7 +869,8 @@ def parallelism(w, n):
     if n == 1:
         return "single GPU"
     if isinstance(w, GemmWorkload) and w.split > 1:
-        return (f"{n} K shards of K = {w.K} on 64-element boundaries, split-K {w.split} within each shard; fp32 "
+        return (f"{n} K shards of K = {w.K} on 64-element boundaries, split-K {shard_splits(w, n)} within each "
+                "shard (every split at least 512 deep); fp32 "
                 "partials summed inside the split-K kernels over peer memory (NVLink) into rank 0's C; one launch "
                 "per GPU per step")
     axis = ("(batch, head) units" if isinstance(w, AttentionWorkload) else
