@@ -204,14 +204,17 @@ __device__ __forceinline__ void atb_store_row(uint32_t taddr, __half* dst) {
 // B_rows^T, A a [128 rows][D] tile and B 64 rows of one, both stored as D/64
 // 64-wide 128-byte-swizzled boxes; `b_addr` points at the unit's first row
 // (tile base + 64 * 128 B for the second half).
+// The descriptors are built once per call: a descriptor's low 14 bits hold
+// (address >> 4), so the k-step offsets are added to it directly.
 template <int D>
 __device__ __forceinline__ void atb_mma_nt_unit(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
   constexpr uint32_t IDESC = idesc_f16_f32(ATT_BM, ATT_BN / 2, false, false);
+  const uint64_t da = sw128_desc(a_addr, 16, 1024);
+  const uint64_t db = sw128_desc(b_addr, 16, 1024);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
-    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-    umma_f16_ss(d_tmem, sw128_desc(a_addr + off, 16, 1024), sw128_desc(b_addr + off, 16, 1024), IDESC,
-                kk > 0 ? 1u : 0u);
+    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+    umma_f16_ss(d_tmem, da + off, db + off, IDESC, kk > 0 ? 1u : 0u);
   }
 }
 
@@ -221,9 +224,10 @@ __device__ __forceinline__ void atb_mma_nt_unit(uint32_t d_tmem, uint32_t a_addr
 template <int D>
 __device__ __forceinline__ void atb_mma_tn_unit(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, bool acc) {
   constexpr uint32_t IDESC = idesc_f16_f32(ATT_BM, D, false, true);
+  const uint64_t db = sw128_desc(b_addr, 16384, 1024);
 #pragma unroll
   for (int kk = 0; kk < ATT_BN / 32; ++kk)
-    umma_f16_ts(d_tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 2048, 16384, 1024), IDESC,
+    umma_f16_ts(d_tmem, a_tmem + kk * 8, db + static_cast<uint32_t>(kk * (2048 >> 4)), IDESC,
                 (acc || kk > 0) ? 1u : 0u);
 }
 
