@@ -9,26 +9,27 @@
 // for head_dim 128 and 64.
 //
 // One CTA per (batch, head, 256 query rows) = two 128-row Q tiles that share
-// every K_j / V_j tile staged in shared memory. 12 warps:
+// every K_j / V_j tile staged in shared memory. Keys are walked in steps of
+// 64 (half a staged tile). 12 warps:
 //   warp 0      TMA producer: Q0, Q1 once, then K_j / V_j (128 keys each) into
 //               rings (128-byte-swizzled boxes of 64 columns x 128 rows).
-//   warp 1      TMEM alloc (512 columns: S0 | S1 | O0 | O1); one elected lane
-//               issues tcgen05.mma. S_i = Q_i K_j^T (M=128, both operands in
-//               smem) is issued in two N = 64 halves; O_i += P_i V_j (M=128,
-//               N=D, K=128) reads P_i from TMEM and V as an MN-major smem
-//               operand. Per key tile: S_lo_0(j+1), PV_0(j), S_lo_1(j+1),
-//               S_hi_0(j+1), PV_1(j), S_hi_1(j+1): while one tile's softmax
-//               runs, the tensor core works on the other tile and on the
-//               first half of this tile's next S.
+//   warp 1      TMEM alloc (512 columns: two 64-column S slots per Q tile,
+//               then O0 | O1).
+//   warps 1, 2  one elected lane each issues Q tile 0's / 1's tcgen05.mma.
+//               S_i(n) = Q_i K(n)^T (M=128, N=64, both operands in smem) goes
+//               to slot n % 2 of tile i; O_i += P_i(n) V(n) (M=128, N=D,
+//               K=64) reads P_i(n) from TMEM and V as an MN-major smem
+//               operand. Per step n: PV_i(n), then S_i(n+2): S runs two steps
+//               ahead of the softmax.
 //   warps 4-7   softmax of Q tile 0, warps 8-11 of Q tile 1: thread r owns
-//               query row r (TMEM lane r). Per key tile it reads its S row
-//               (tcgen05.ld), releases the S columns, forms P = 2^(s - m)
-//               against the running max m while taking the new row max,
-//               writes P as fp16 pairs into the upper half of its S row
-//               (tcgen05.st), and only when the max grew by more than 8 in
-//               the log2 domain (a factor of 256) rescales its O row in TMEM
-//               and its running sum l and redoes P (lazy rescaling). At the
-//               end it reads O, multiplies by 1/l and stores fp16.
+//               query row r (TMEM lane r). Per step it reads its 64 scores
+//               (tcgen05.ld), forms P = 2^(s - m) against the running max m
+//               while taking the new row max, writes P as fp16 pairs over the
+//               first half of the step's slot (tcgen05.st), and only when the
+//               max grew by more than 8 in the log2 domain (a factor of 256)
+//               rescales its O row in TMEM and its running sum l and redoes P
+//               (lazy rescaling). At the end it reads O, multiplies by 1/l and
+//               stores fp16.
 // Keys past the sequence end are masked to -inf; query rows past the end are
 // computed on zero-filled Q and not stored.
 #pragma once
@@ -40,6 +41,8 @@ namespace mm4 {
 struct AttnArgs {
   int batch, heads_q, heads_kv, R, C;  // R = query rows, C = key/value rows
   int layout;                           // 0: [B][H][S][D], 1: [B][S][H][D]
+  int q_blocks;                         // 256-row query blocks per (batch, head)
+  int num_units;                        // batch * heads_q * q_blocks
   float scale_log2;                     // scale * log2(e)
   __half* O;
   float* lse;                           // optional [B][Hq][R]: natural-log sum of exp(scale * S) per row
@@ -51,7 +54,8 @@ constexpr int ATT_D = 128;
 constexpr int ATT_BM = 128;                     // query rows per Q tile
 constexpr int ATT_QTILES = 2;                   // Q tiles per CTA
 constexpr int ATT_CTA_ROWS = ATT_BM * ATT_QTILES;
-constexpr int ATT_BN = 128;                     // keys per tile
+constexpr int ATT_BN = 128;                     // keys per staged K / V tile
+constexpr int ATT_SN = 64;                      // keys per softmax step (half a staged tile)
 constexpr int ATT_THREADS = 384;
 constexpr int ATT_TILE_BYTES = 128 * 128 * 2;   // 32 KB: one head-dim-128 Q, K_j or V_j tile
 // Register split: warps 0-3 (producer, MMA, two idle) give registers to the
@@ -73,6 +77,7 @@ enum : int {
   SITE_ATT_SOFTMAX_O = 49,
   SITE_ATT_MMA_S = 50,
   SITE_ATT_MMA_PV = 51,
+  SITE_ATT_MMA_O = 52,
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -105,12 +110,6 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23) + bias));
 }
 
-// Of every 8 consecutive scores of a row, this many (an even number) take the
-// FMA-pipe exponential and the rest the hardware ex2.
-#ifndef ATT_EMU_PER8
-#define ATT_EMU_PER8 2
-#endif
-
 // Per-head-dim constants of the forward kernel. A tile is 128 rows x D
 // fp16, loaded as D/64 boxes of 64 columns (128-byte swizzle); TMEM holds
 // S0 | S1 (128 columns each) then O0 | O1 (D columns each).
@@ -122,6 +121,12 @@ struct AttFwdCfg {
   static constexpr int K_STAGES = (D == 128) ? 3 : 4;
   static constexpr int V_STAGES = (D == 128) ? 2 : 4;
   static constexpr int SMEM_BYTES = (ATT_QTILES + K_STAGES + V_STAGES) * TILE_BYTES + 512 + 1024;
+  // Exponentials per 8 on the FMA pipe. At D = 128 the tensor work per key
+  // step leaves the softmax slack, and the MUFU-only loop (fewer
+  // instructions) is faster; at D = 64 the softmax bounds the step and
+  // moving 2 of 8 off MUFU pays (B4 H16 S4096 on one B200: D = 128 0.449 ms
+  // with 0, 0.464 with 2; D = 64 0.360 ms with 2, 0.374 with 0).
+  static constexpr int EMU_PER8 = (D == 128) ? 0 : 2;
 };
 
 // Loads one 128-row tile of head dim D (D/64 boxes of 64 columns).
@@ -137,38 +142,39 @@ __device__ __forceinline__ void att_load_tile_d(const CUtensorMap* map, uint64_t
   }
 }
 
-// Row maximum of 128 raw scores: four independent chains of three-input
-// maxima (x[0..3] start them, 4..123 join eight at a time, 124..127 last).
-__device__ __forceinline__ float att_row_max(const float (&x)[128]) {
+// Row maximum of the 64 raw scores of one key step: four independent chains
+// of three-input maxima (x[0..3] start them, 4..59 join eight at a time,
+// 60..63 last).
+__device__ __forceinline__ float att_row_max64(const float (&x)[64]) {
   float pm[4] = {x[0], x[1], x[2], x[3]};
 #pragma unroll
-  for (int i = 4; i < 124; i += 8)
+  for (int i = 4; i < 60; i += 8)
 #pragma unroll
     for (int e = 0; e < 4; ++e) pm[e] = fmax3(pm[e], x[i + e], x[i + 4 + e]);
-  return fmax3(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]), fmaxf(fmaxf(x[124], x[125]), fmaxf(x[126], x[127])));
+  return fmax3(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]), fmaxf(fmaxf(x[60], x[61]), fmaxf(x[62], x[63])));
 }
 
-// P = 2^(x * scale_log2 - m) for the 128 scores of this thread's row: one
-// packed FFMA per pair, ATT_EMU_PER8 of every 8 exponentials on the FMA pipe
-// and the rest on MUFU, packed partial sums. P is written as fp16 pairs into
-// the 64 TMEM columns at tP (the upper half of the row's S columns), 16 at a
-// time. Returns
-// the row's partial sum of P.
-__device__ __forceinline__ float att_exp_store(const float (&x)[128], float sl2, float m, uint32_t tP) {
+// P = 2^(x * scale_log2 - m) for the 64 scores of this thread's row in one
+// key step: one packed FFMA per pair, EMU of every 8 exponentials on the FMA
+// pipe and the rest on MUFU, packed partial sums. P is written as fp16 pairs
+// into the 32 TMEM columns at tP, 16 at a time. Returns the row's partial sum
+// of P.
+template <int EMU>
+__device__ __forceinline__ float att_exp_store64(const float (&x)[64], float sl2, float m, uint32_t tP) {
   const float2 sc = make_float2(sl2, sl2);
   const float2 nm = make_float2(-m, -m);
   float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-  for (int quarter = 0; quarter < 4; ++quarter) {
+  for (int half = 0; half < 2; ++half) {
     uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int idx = quarter * 32 + c * 8 + 2 * e;
+        const int idx = half * 32 + c * 8 + 2 * e;
         const float2 a = ffma2(make_float2(x[idx], x[idx + 1]), sc, nm);
         float2 pv;
-        if (2 * e >= 8 - ATT_EMU_PER8) {
+        if (2 * e >= 8 - EMU) {
           pv = ex2_poly2(a);
         } else {
           pv.x = ex2_approx(a.x);
@@ -178,7 +184,7 @@ __device__ __forceinline__ float att_exp_store(const float (&x)[128], float sl2,
         pk[c * 4 + e] = pack_half2(pv.x, pv.y);
       }
     }
-    tmem_st_32x32b_x16(tP + quarter * 16, pk);
+    tmem_st_32x32b_x16(tP + half * 16, pk);
   }
   const float2 s01 = fadd2(fadd2(acc[0], acc[1]), fadd2(acc[2], acc[3]));
   return s01.x + s01.y;
@@ -186,22 +192,31 @@ __device__ __forceinline__ float att_exp_store(const float (&x)[128], float sl2,
 
 // Flash-attention forward, head dim D (64 or 128); see the file comment.
 //
-// TMEM per Q tile i: S_i in columns [128 i, 128 i + 128), O_i in
-// [256 + D i, 256 + D (i + 1)). S_i(j) = Q_i K_j^T is issued as two N = 64
-// halves: S_lo (keys 0-63 -> columns 0-63) and S_hi (keys 64-127 -> columns
-// 64-127). The softmax writes P_i(j) as fp16 pairs into columns 64-127 (over
-// S_hi), which O_i += P_i(j) V_j reads. So:
-//   - S_lo_i(j+1) only needs the softmax to have loaded S_i(j) into registers
-//     (s_read); it runs on the tensor core while the softmax computes P_i(j);
-//   - S_hi_i(j+1) overwrites P_i(j): it is issued only after the commit of
-//     O_i += P_i(j) V_j has completed (pv_done), which orders the read of P
-//     before the overwrite through an mbarrier rather than through the
-//     issue order of MMAs on different accumulators.
+// Persistent: CTA c takes the units (batch, head, 256 query rows) c, c + G,
+// c + 2G, ... (G = gridDim.x), and every role walks them in order, so the
+// next unit's Q / K / V loads and first S MMAs overlap the current unit's
+// last steps and epilogue. Steps are counted across units (g), which fixes
+// the TMEM slot (g % 2) and the mbarrier phases of every per-step barrier.
+//
+// Keys are walked in steps of 64 (half a staged K_j / V_j tile). TMEM per Q
+// tile i: two 64-column slots, [128 i, 128 i + 64) and [128 i + 64,
+// 128 i + 128); S_i(g) = Q_i K(g)^T goes to slot g % 2, and the softmax
+// writes P_i(g) as fp16 pairs over the first 32 columns of the same slot.
+// O_i is in [256 + D i, 256 + D (i + 1)). The MMA issuer keeps S two steps
+// ahead: S_i(g + 2) reuses slot g % 2 and is issued once the commit of
+// O_i += P_i(g) V(g) has completed (pv_done), so the read of P_i(g) is
+// ordered before the overwrite through an mbarrier, not through the issue
+// order of MMAs on different accumulators. The softmax of step g + 1 then
+// finds S_i(g + 1) ready and never waits for its own P.V. The first P.V of
+// a unit overwrites O_i only after the softmax has read the previous unit's
+// O_i (o_empty); a unit's Q_i is replaced only after its last S_i (q_empty).
+//
 // Each softmax row takes its exponentials against the running max of the
-// previous key tiles while the row max of the new tile is formed alongside
-// them; only when the max grew by more than 8 (log2 domain) are O and l
-// rescaled and the exponentials redone against the new max (lazy rescaling:
-// the stale max cancels exactly in O / l).
+// previous steps while the row max of the new step is formed alongside them;
+// only when the max grew by more than 8 (log2 domain) are O and l rescaled
+// and the exponentials redone against the new max (lazy rescaling: the stale
+// max cancels exactly in O / l). The rescale first waits for the previous
+// step's P.V (pv_done), the only MMA that can still be writing O_i.
 template <int D>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -210,8 +225,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   constexpr int KS = Cfg::K_STAGES;
   constexpr int VS = Cfg::V_STAGES;
   constexpr int TB = Cfg::TILE_BYTES;
-  constexpr uint32_t IDESC_S = idesc_f16_f32(ATT_BM, ATT_BN, false, false);
-  constexpr uint32_t IDESC_S_HALF = idesc_f16_f32(ATT_BM, ATT_BN / 2, false, false);
+  constexpr uint32_t IDESC_S = idesc_f16_f32(ATT_BM, ATT_SN, false, false);
   constexpr uint32_t IDESC_O = idesc_f16_f32(ATT_BM, D, false, true);
 
   extern __shared__ uint8_t smem_raw[];
@@ -221,14 +235,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* sK = smem + ATT_QTILES * TB;                        // [KS]
   uint8_t* sV = sK + KS * TB;                                  // [VS]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VS * TB);
-  uint64_t* q_full = bars;                  // 2
-  uint64_t* s_full = bars + 2;              // 2: S_i(j) complete in TMEM
-  uint64_t* s_read = bars + 4;              // 2: the softmax holds S_i(j) in registers
-  uint64_t* p_full = bars + 6;              // 2: P_i(j) in TMEM (and O_i rescaled)
-  uint64_t* pv_done = bars + 8;             // 2: O_i += P_i(j) V_j complete
-  uint64_t* o_full = bars + 10;             // 2: last O_i += P V complete
-  uint64_t* drain = bars + 12;              // 1
-  uint64_t* k_full = bars + 13;             // KS
+  uint64_t* q_full = bars;                  // [tile]: Q_i of the unit landed
+  uint64_t* q_empty = bars + 2;             // [tile]: the unit's last S_i complete
+  uint64_t* s_full = bars + 4;              // [tile][slot]: S_i(g) complete in TMEM
+  uint64_t* p_full = bars + 8;              // [tile][slot]: P_i(g) in TMEM (and O_i rescaled)
+  uint64_t* pv_done = bars + 12;            // [tile][slot]: O_i += P_i(g) V(g) complete
+  uint64_t* o_full = bars + 16;             // [tile]: the unit's last O_i += P V complete
+  uint64_t* o_empty = bars + 18;            // [tile]: the softmax holds the unit's O_i in registers
+  uint64_t* drain = bars + 20;              // 1
+  uint64_t* k_full = bars + 21;             // KS
   uint64_t* k_empty = k_full + KS;          // KS
   uint64_t* v_full = k_empty + KS;          // VS
   uint64_t* v_empty = v_full + VS;          // VS
@@ -237,28 +252,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const Watchdog wd{args.status, args.timeout_ns};
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int hk = h / (args.heads_q / args.heads_kv);
-  const int nkv = (args.C + ATT_BN - 1) / ATT_BN;
+  const int nkv = (args.C + ATT_BN - 1) / ATT_BN;   // staged K / V tiles per unit
+  const int nst = (args.C + ATT_SN - 1) / ATT_SN;   // key steps per unit
+  const int units = (args.num_units - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                    static_cast<int>(gridDim.x);     // units of this CTA
+  const int total = units * nst;                    // key steps of this CTA
+  // (query block, head, batch) of this CTA's unit ul
+  auto unit_of = [&](int ul, int& qb, int& h, int& b) {
+    const int u = static_cast<int>(blockIdx.x) + ul * static_cast<int>(gridDim.x);
+    qb = u % args.q_blocks;
+    const int bh = u / args.q_blocks;
+    h = bh % args.heads_q;
+    b = bh / args.heads_q;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_read[i], ATT_BM);
-      mbar_init(&p_full[i], ATT_BM);
-      mbar_init(&pv_done[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], ATT_BM);
+      for (int sl = 0; sl < 2; ++sl) {
+        mbar_init(&s_full[2 * i + sl], 1);
+        mbar_init(&p_full[2 * i + sl], ATT_BM);
+        mbar_init(&pv_done[2 * i + sl], 1);
+      }
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+      mbar_init(&k_empty[i], 2);
     }
     for (int i = 0; i < VS; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&v_empty[i], 2);
     }
     fence_mbar_init();
   }
@@ -279,139 +306,142 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      const int row0 = blockIdx.x * ATT_CTA_ROWS;
-      mbar_arrive_expect_tx(&q_full[0], TB);
-      att_load_tile_d<D>(&tmQ, &q_full[0], sQ, args.layout, row0, h, b);
-      int kj = 0, vj = 0;  // tiles issued
-      for (int j = 0; j < nkv; ++j) {
-        const int ks = j % KS;
-        if (!mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, wd, SITE_ATT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&k_full[ks], TB);
-        att_load_tile_d<D>(&tmK, &k_full[ks], sK + ks * TB, args.layout, j * ATT_BN, hk, b);
-        kj = j + 1;
-        if (j == 0) {
-          mbar_arrive_expect_tx(&q_full[1], TB);
-          att_load_tile_d<D>(&tmQ, &q_full[1], sQ + TB, args.layout, row0 + ATT_BM, h, b);
+      int nq[2] = {0, 0};  // Q loads issued per tile
+      int kt = 0, vt = 0;  // K / V tiles issued (ring positions)
+      bool ok = true;
+      for (int ul = 0; ul < units && ok; ++ul) {
+        int qb, h, b;
+        unit_of(ul, qb, h, b);
+        const int hk = h / (args.heads_q / args.heads_kv);
+        const int row0 = qb * ATT_CTA_ROWS;
+        for (int j = 0; j < nkv && ok; ++j) {
+          // Q_0 before the unit's first K tile, Q_1 after it; each waits for
+          // the previous unit's last S_i.
+          for (int i = 0; i < 2 && j == 0; ++i) {
+            if (i == 1) {
+              const int ks = kt % KS;
+              if (!(ok = mbar_wait(&k_empty[ks], ((kt / KS) & 1) ^ 1, wd, SITE_ATT_PRODUCER))) break;
+              mbar_arrive_expect_tx(&k_full[ks], TB);
+              att_load_tile_d<D>(&tmK, &k_full[ks], sK + ks * TB, args.layout, 0, hk, b);
+              ++kt;
+            }
+            if (ul > 0 && !(ok = mbar_wait(&q_empty[i], (ul - 1) & 1, wd, SITE_ATT_PRODUCER))) break;
+            mbar_arrive_expect_tx(&q_full[i], TB);
+            att_load_tile_d<D>(&tmQ, &q_full[i], sQ + i * TB, args.layout, row0 + i * ATT_BM, h, b);
+            ++nq[i];
+          }
+          if (!ok) break;
+          if (j > 0) {
+            const int ks = kt % KS;
+            if (!(ok = mbar_wait(&k_empty[ks], ((kt / KS) & 1) ^ 1, wd, SITE_ATT_PRODUCER))) break;
+            mbar_arrive_expect_tx(&k_full[ks], TB);
+            att_load_tile_d<D>(&tmK, &k_full[ks], sK + ks * TB, args.layout, j * ATT_BN, hk, b);
+            ++kt;
+          }
+          const int vs = vt % VS;
+          if (!(ok = mbar_wait(&v_empty[vs], ((vt / VS) & 1) ^ 1, wd, SITE_ATT_PRODUCER))) break;
+          mbar_arrive_expect_tx(&v_full[vs], TB);
+          att_load_tile_d<D>(&tmV, &v_full[vs], sV + vs * TB, args.layout, j * ATT_BN, hk, b);
+          ++vt;
         }
-        const int vs = j % VS;
-        if (!mbar_wait(&v_empty[vs], ((j / VS) & 1) ^ 1, wd, SITE_ATT_PRODUCER)) break;
-        mbar_arrive_expect_tx(&v_full[vs], TB);
-        att_load_tile_d<D>(&tmV, &v_full[vs], sV + vs * TB, args.layout, j * ATT_BN, hk, b);
-        vj = j + 1;
       }
       // Wait for the last copy into every buffer before leaving.
-      mbar_wait(&q_full[0], 0, wd, SITE_ATT_PRODUCER_DRAIN);
-      if (kj > 0) mbar_wait(&q_full[1], 0, wd, SITE_ATT_PRODUCER_DRAIN);
-      for (int i = (kj > KS ? kj - KS : 0); i < kj; ++i)
-        mbar_wait(&k_full[i % KS], (i / KS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
-      for (int i = (vj > VS ? vj - VS : 0); i < vj; ++i)
-        mbar_wait(&v_full[i % VS], (i / VS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
+      for (int i = 0; i < 2; ++i)
+        if (nq[i] > 0) mbar_wait(&q_full[i], (nq[i] - 1) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
+      for (int t = (kt > KS ? kt - KS : 0); t < kt; ++t)
+        mbar_wait(&k_full[t % KS], (t / KS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
+      for (int t = (vt > VS ? vt - VS : 0); t < vt; ++t)
+        mbar_wait(&v_full[t % VS], (t / VS) & 1, wd, SITE_ATT_PRODUCER_DRAIN);
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ---------------------------------------------------------- MMA issuers
+    // Warp 1 issues Q tile 0's MMAs, warp 2 Q tile 1's: one thread issues
+    // about one tcgen05.mma per 55 SM clocks, so a single issuer could not
+    // keep the tensor core fed with N = 64 S MMAs.
     if (elect_one()) {
+      const int i = warp - 1;
       // Shared-memory descriptors of the tile bases; a descriptor's low 14
-      // bits hold (address >> 4), so the k-step offsets inside a tile are
-      // added to it directly (every address stays below 256 KB).
+      // bits hold (address >> 4), so the offsets inside a tile are added to
+      // it directly (every address stays below 256 KB).
       const uint64_t q_desc0 = sw128_desc(smem_u32(sQ), 16, 1024);
       const uint64_t k_desc0 = sw128_desc(smem_u32(sK), 16, 1024);
       const uint64_t v_desc0 = sw128_desc(smem_u32(sV), 16384, 1024);
-      // S_i = Q_i K^T of key stage ks: part 0 = keys 0-63 into columns 0-63,
-      // part 1 = keys 64-127 into columns 64-127, part 2 = all 128 keys.
-      auto issue_s = [&](int i, int ks, int part) {
+      // The last step of a unit that reads a staged K / V tile.
+      auto last_step_of_tile = [&](int n) { return (n & 1) == 1 || n == nst - 1; };
+      // Position of a key step: g counts steps across units, n within unit
+      // ul; t is the staged K / V tile (ring position) the step reads. Kept
+      // incrementally: the issuing thread's index arithmetic sits between
+      // MMA groups.
+      struct Pos {
+        int g, ul, n, t;
+      };
+      auto advance = [&](Pos& p) {
+        ++p.g;
+        if (++p.n == nst) {
+          p.n = 0;
+          ++p.ul;
+          p.t = p.ul * nkv;
+        } else if ((p.n & 1) == 0) {
+          ++p.t;
+        }
+      };
+      // S_i(g) = Q_i K(g)^T: the 64 keys of step n are rows 64 (n % 2) .. +64
+      // of the unit's staged K tile n / 2 (8 KB into each 64-column box).
+      // Waits for the unit's Q_i (first step), the K tile (first of its two
+      // steps) and the slot (P.V of step g - 2).
+      auto do_s = [&](int i, const Pos& p) -> bool {
+        const int g = p.g, n = p.n, ks = p.t % KS;
+        if (n == 0 && !mbar_wait(&q_full[i], p.ul & 1, wd, SITE_ATT_MMA_Q)) return false;
+        if ((n & 1) == 0 && !mbar_wait(&k_full[ks], (p.t / KS) & 1, wd, SITE_ATT_MMA_K)) return false;
+        if (g >= 2 && !mbar_wait(&pv_done[2 * i + (g & 1)], ((g - 2) >> 1) & 1, wd, SITE_ATT_MMA_PV)) return false;
+        tc_fence_after();
         const uint64_t qd = q_desc0 + static_cast<uint32_t>(i * (TB >> 4));
-        const uint64_t kd = k_desc0 + static_cast<uint32_t>((ks * TB + (part == 1 ? 8192 : 0)) >> 4);
-        const uint32_t d_tmem = tmem_base + i * 128 + (part == 1 ? 64u : 0u);
-        const uint32_t idesc = part == 2 ? IDESC_S : IDESC_S_HALF;
+        const uint64_t kd = k_desc0 + static_cast<uint32_t>((ks * TB + (n & 1) * 8192) >> 4);
+        const uint32_t d_tmem = tmem_base + i * 128 + (g & 1) * ATT_SN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-          umma_f16_ss(d_tmem, qd + off, kd + off, idesc, kk > 0 ? 1u : 0u);
+          umma_f16_ss(d_tmem, qd + off, kd + off, IDESC_S, kk > 0 ? 1u : 0u);
         }
+        umma_commit(&s_full[2 * i + (g & 1)]);
+        if (n == nst - 1) umma_commit(&q_empty[i]);
+        if (last_step_of_tile(n)) umma_commit(&k_empty[ks]);
+        return true;
       };
-      // O_i += P_i V: P_i is fp16 pairs in TMEM columns [128 i + 64, 128 i + 128).
-      auto issue_pv = [&](int i, int vs, bool acc) {
-        const uint64_t vd = v_desc0 + static_cast<uint32_t>((vs * TB) >> 4);
+      // O_i += P_i(g) V(g): P_i(g) is fp16 pairs in the first 32 columns of
+      // slot g % 2; V(g) is rows 64 (n % 2) .. +64 of the unit's staged V
+      // tile n / 2. A unit's first P.V starts O_i afresh, once the softmax
+      // has read the previous unit's O_i.
+      auto do_pv = [&](int i, const Pos& p) -> bool {
+        const int g = p.g, n = p.n, vs = p.t % VS;
+        if (!mbar_wait(&p_full[2 * i + (g & 1)], (g >> 1) & 1, wd, SITE_ATT_MMA_P)) return false;
+        if ((n & 1) == 0 && !mbar_wait(&v_full[vs], (p.t / VS) & 1, wd, SITE_ATT_MMA_V)) return false;
+        if (n == 0 && p.ul > 0 && !mbar_wait(&o_empty[i], (p.ul - 1) & 1, wd, SITE_ATT_MMA_O)) return false;
+        tc_fence_after();
+        const uint64_t vd = v_desc0 + static_cast<uint32_t>((vs * TB + (n & 1) * 8192) >> 4);
         const uint32_t d_tmem = tmem_base + 256 + i * D;
-        const uint32_t p_tmem = tmem_base + i * 128 + 64;
+        const uint32_t p_tmem = tmem_base + i * 128 + (g & 1) * ATT_SN;
 #pragma unroll
-        for (int kk = 0; kk < ATT_BN / 16; ++kk)
+        for (int kk = 0; kk < ATT_SN / 16; ++kk)
           umma_f16_ts(d_tmem, p_tmem + kk * 8, vd + static_cast<uint32_t>(kk * (2048 >> 4)), IDESC_O,
-                      (acc || kk > 0) ? 1u : 0u);
+                      (n > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[2 * i + (g & 1)]);
+        if (n == nst - 1) umma_commit(&o_full[i]);
+        if (last_step_of_tile(n)) umma_commit(&v_empty[vs]);
+        return true;
       };
-      bool ok = mbar_wait(&q_full[0], 0, wd, SITE_ATT_MMA_Q) && mbar_wait(&k_full[0], 0, wd, SITE_ATT_MMA_K);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0, 2);
-        umma_commit(&s_full[0]);
-        ok = mbar_wait(&q_full[1], 0, wd, SITE_ATT_MMA_Q);
-      }
-      if (ok) {
-        tc_fence_after();
-        issue_s(1, 0, 2);
-        umma_commit(&s_full[1]);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int vs = j % VS;
-        const bool more = j + 1 < nkv;
-        const int ks = (j + 1) % KS;
-        const uint32_t par = static_cast<uint32_t>(j & 1);
-        // Tile 0: keys 0-63 of the next S while its softmax forms P_0(j).
-        if (more) {
-          if (!mbar_wait(&s_read[0], par, wd, SITE_ATT_MMA_S) ||
-              !mbar_wait(&k_full[ks], ((j + 1) / KS) & 1, wd, SITE_ATT_MMA_K)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(0, ks, 0);
-        }
-        // Tile 0: O_0 += P_0(j) V_j.
-        if (!mbar_wait(&p_full[0], par, wd, SITE_ATT_MMA_P) ||
-            !mbar_wait(&v_full[vs], (j / VS) & 1, wd, SITE_ATT_MMA_V)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_pv(0, vs, j > 0);
-        umma_commit(more ? &pv_done[0] : &o_full[0]);
-        // Tile 1: keys 0-63 of the next S.
-        if (more) {
-          if (!mbar_wait(&s_read[1], par, wd, SITE_ATT_MMA_S)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(1, ks, 0);
-          // Tile 0: keys 64-127 of the next S, over P_0(j) once O_0 += P_0(j) V_j is done.
-          if (!mbar_wait(&pv_done[0], par, wd, SITE_ATT_MMA_PV)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(0, ks, 1);
-          umma_commit(&s_full[0]);
-        }
-        // Tile 1: O_1 += P_1(j) V_j.
-        if (!mbar_wait(&p_full[1], par, wd, SITE_ATT_MMA_P)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        issue_pv(1, vs, j > 0);
-        umma_commit(&v_empty[vs]);
-        umma_commit(more ? &pv_done[1] : &o_full[1]);
-        if (more) {
-          if (!mbar_wait(&pv_done[1], par, wd, SITE_ATT_MMA_PV)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_s(1, ks, 1);
-          umma_commit(&s_full[1]);
-          umma_commit(&k_empty[ks]);
-        }
+      const Pos first{0, 0, 0, 0};
+      Pos second = first;
+      advance(second);
+      bool ok = do_s(i, first) && (total < 2 || do_s(i, second));
+      // Per step g: this tile's P.V, then S_i(g + 2) into the slot that P.V
+      // frees. While this issuer waits for the P.V to complete, the other
+      // tile's issuer keeps the tensor core busy.
+      Pos pv = first, sx = second;
+      advance(sx);
+      for (; pv.g < total && ok; advance(pv), advance(sx)) {
+        ok = do_pv(i, pv);
+        if (ok && sx.g < total) ok = do_s(i, sx);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, wd, SITE_ATT_MMA_DRAIN);
@@ -425,112 +455,116 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tS = tmem_base + ti * 128 + lane_off;
-    const uint32_t tP = tS + 64;
     const uint32_t tO = tmem_base + 256 + ti * D + lane_off;
     const float sl2 = args.scale_log2;
-    float m = -INFINITY;  // running max, log2 domain (possibly stale by < 8)
-    float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[ti], j & 1, wd, SITE_ATT_SOFTMAX_S));
+    int g = 0;  // key steps done, across units
+    for (int ul = 0; ul < units && ok; ++ul) {
+      float m = -INFINITY;  // running max, log2 domain (possibly stale by < 8)
+      float l = 0.f;
+      for (int n = 0; n < nst; ++n, ++g) {
+        const int sl = g & 1;
+        const uint32_t tSl = tS + sl * ATT_SN;
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[2 * ti + sl], (g >> 1) & 1, wd, SITE_ATT_SOFTMAX_S));
+        if (!ok) break;
+        tc_fence_after();
+        float x[64];
+        {
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(tSl + 0, v0);
+          tmem_ld_32x32b_x32(tSl + 32, v1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            x[i] = __uint_as_float(v0[i]);
+            x[32 + i] = __uint_as_float(v1[i]);
+          }
+        }
+        const int valid = args.C - n * ATT_SN;
+        if (valid < ATT_SN) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= valid) x[i] = -INFINITY;
+        }
+        float part;
+        if (n == 0) {
+          m = att_row_max64(x) * sl2;
+          part = att_exp_store64<Cfg::EMU_PER8>(x, sl2, m, tSl);
+        } else {
+          // Exponentials against the running max, the new row max alongside.
+          part = att_exp_store64<Cfg::EMU_PER8>(x, sl2, m, tSl);
+          const float mx = att_row_max64(x) * sl2;
+          const bool grow = (mx > m + 8.0f);
+          if (__any_sync(0xffffffffu, grow)) {
+            // Rescale this warp's O rows in TMEM (lanes without growth use
+            // 1.0) and redo the exponentials against the new max, once the
+            // previous step's O_i += P V (the only MMA that may still write
+            // O_i) is done.
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(&pv_done[2 * ti + (sl ^ 1)], ((g - 1) >> 1) & 1, wd, SITE_ATT_SOFTMAX_O));
+            if (!ok) break;
+            tc_fence_after();
+            const float m_new = grow ? mx : m;
+            const float factor = grow ? ex2_approx(m - m_new) : 1.0f;
+#pragma unroll 1
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t v[16];
+              tmem_ld_32x32b_x16(tO + c * 16, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * factor);
+              tmem_st_32x32b_x16(tO + c * 16, v);
+            }
+            l *= factor;
+            m = m_new;
+            tmem_st_wait();
+            part = att_exp_store64<Cfg::EMU_PER8>(x, sl2, m, tSl);
+          }
+        }
+        l += part;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[2 * ti + sl]);
+      }
+      if (!ok) break;
+      // Epilogue of the unit: O_i into registers (then its TMEM columns may
+      // take the next unit's first P.V), times 1/l, fp16 stores.
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_full[ti], ul & 1, wd, SITE_ATT_SOFTMAX_O));
       if (!ok) break;
       tc_fence_after();
-      float x[128];
-      {
-        uint32_t v0[32], v1[32], v2[32], v3[32];
-        tmem_ld_32x32b_x32(tS + 0, v0);
-        tmem_ld_32x32b_x32(tS + 32, v1);
-        tmem_ld_32x32b_x32(tS + 64, v2);
-        tmem_ld_32x32b_x32(tS + 96, v3);
-        tmem_ld_wait();
+      uint32_t o[D];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[i] = __uint_as_float(v0[i]);
-          x[32 + i] = __uint_as_float(v1[i]);
-          x[64 + i] = __uint_as_float(v2[i]);
-          x[96 + i] = __uint_as_float(v3[i]);
-        }
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t* oc = o + c * 32;
+        tmem_ld_32x32b_x32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(oc));
       }
-      // S_i(j) is in registers: its TMEM columns may take the next S_lo.
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s_read[ti]);
-      const int valid = args.C - j * ATT_BN;
-      if (valid < ATT_BN) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= valid) x[i] = -INFINITY;
+      mbar_arrive(&o_empty[ti]);
+      int qb, h, b;
+      unit_of(ul, qb, h, b);
+      const int row = qb * ATT_CTA_ROWS + ti * ATT_BM + r;
+      const float inv_l = 1.0f / l;
+      if (args.lse != nullptr && row < args.R) {
+        // m and l share the same (possibly stale) max, so m + log2(l) is the
+        // row's log2-sum-exp2 of scale*log2(e)*S; times ln 2 gives the
+        // natural-log value (Network.swift createLTerm).
+        args.lse[(static_cast<long long>(b) * args.heads_q + h) * args.R + row] =
+            (m + log2f(l)) * 0.6931471805599453f;
       }
-      float part;
-      if (j == 0) {
-        m = att_row_max(x) * sl2;
-        part = att_exp_store(x, sl2, m, tP);
-      } else {
-        // Exponentials against the running max, the new row max alongside.
-        part = att_exp_store(x, sl2, m, tP);
-        const float mx = att_row_max(x) * sl2;
-        const bool grow = (mx > m + 8.0f);
-        if (__any_sync(0xffffffffu, grow)) {
-          // Rescale this warp's O rows in TMEM (lanes without growth use 1.0)
-          // and redo the exponentials against the new max. The last
-          // O_i += P_i(j-1) V has completed: the commit of S_i(j) covers it.
-          const float m_new = grow ? mx : m;
-          const float factor = grow ? ex2_approx(m - m_new) : 1.0f;
-#pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(tO + c * 16, v);
-            tmem_ld_wait();
+      if (row < args.R) {
+        const long long off = (args.layout == 0)
+                                  ? ((static_cast<long long>(b) * args.heads_q + h) * args.R + row) * D
+                                  : ((static_cast<long long>(b) * args.R + row) * args.heads_q + h) * D;
+        __half* dst = args.O + off;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * factor);
-            tmem_st_32x32b_x16(tO + c * 16, v);
-          }
-          l *= factor;
-          m = m_new;
-          tmem_st_wait();
-          part = att_exp_store(x, sl2, m, tP);
-        }
-      }
-      l += part;
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[ti]);
-    }
-    if (ok) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&o_full[ti], 0, wd, SITE_ATT_SOFTMAX_O));
-      if (ok) {
-        tc_fence_after();
-        const int row = blockIdx.x * ATT_CTA_ROWS + ti * ATT_BM + r;
-        const float inv_l = 1.0f / l;
-        if (args.lse != nullptr && row < args.R) {
-          // m and l share the same (possibly stale) max, so m + log2(l) is
-          // the row's log2-sum-exp2 of scale*log2(e)*S; times ln 2 gives the
-          // natural-log value (Network.swift createLTerm).
-          args.lse[(static_cast<long long>(b) * args.heads_q + h) * args.R + row] =
-              (m + log2f(l)) * 0.6931471805599453f;
-        }
-        __half* dst = nullptr;
-        if (row < args.R) {
-          const long long off = (args.layout == 0)
-                                    ? ((static_cast<long long>(b) * args.heads_q + h) * args.R + row) * D
-                                    : ((static_cast<long long>(b) * args.R + row) * args.heads_q + h) * D;
-          dst = args.O + off;
-        }
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tO + c * 32, v);
-          tmem_ld_wait();
-          if (dst) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 pk;
-              pk.x = pack_half2(__uint_as_float(v[i]) * inv_l, __uint_as_float(v[i + 1]) * inv_l);
-              pk.y = pack_half2(__uint_as_float(v[i + 2]) * inv_l, __uint_as_float(v[i + 3]) * inv_l);
-              pk.z = pack_half2(__uint_as_float(v[i + 4]) * inv_l, __uint_as_float(v[i + 5]) * inv_l);
-              pk.w = pack_half2(__uint_as_float(v[i + 6]) * inv_l, __uint_as_float(v[i + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(dst + c * 32 + i) = pk;
-            }
-          }
+        for (int i = 0; i < D; i += 8) {
+          uint4 pk;
+          pk.x = pack_half2(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l);
+          pk.y = pack_half2(__uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+          pk.z = pack_half2(__uint_as_float(o[i + 4]) * inv_l, __uint_as_float(o[i + 5]) * inv_l);
+          pk.w = pack_half2(__uint_as_float(o[i + 6]) * inv_l, __uint_as_float(o[i + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(dst + i) = pk;
         }
       }
     }

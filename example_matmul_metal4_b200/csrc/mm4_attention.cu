@@ -75,7 +75,7 @@ namespace {
 
 template <int D>
 mm4_status launch_forward(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& args,
-                          const mm4_attention_desc& d, cudaStream_t st, int duplicated_count) {
+                          const mm4_attention_desc& d, int sm_count, cudaStream_t st, int duplicated_count) {
   const void* kern = reinterpret_cast<const void*>(attention_fwd_sm100_kernel<D>);
   constexpr int smem = AttFwdCfg<D>::SMEM_BYTES;
   mm4_status rc = ensure_smem_attr(kern, smem);
@@ -94,8 +94,11 @@ mm4_status launch_forward(const CUtensorMap& tq, const CUtensorMap& tk, const CU
       return fail(MM4_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs %d", launch_regs,
                   ATT_REGS_NEEDED);
   }
-  dim3 grid((d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS, d.heads_q, d.batch);
-  if (grid.y > 65535 || grid.z > 65535) return fail(MM4_ERR_UNSUPPORTED, "too many heads or batches for one launch");
+  // Persistent: one CTA per SM at most, each walking units (batch, head,
+  // 256 query rows) gridDim.x apart.
+  const long long units = static_cast<long long>(args.q_blocks) * d.heads_q * d.batch;
+  if (units > 0x7fffffffLL) return fail(MM4_ERR_UNSUPPORTED, "too many query blocks for one launch");
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(units, sm_count)));
   for (int i = 0; i < duplicated_count; ++i) {
     attention_fwd_sm100_kernel<D><<<grid, ATT_THREADS, smem, st>>>(tq, tk, tv, args);
     cudaError_t e = cudaGetLastError();
@@ -131,14 +134,17 @@ mm4_status attention_forward(const mm4_attention_plan* p, const void* Q, const v
   args.R = d.rows;
   args.C = d.columns;
   args.layout = d.layout;
+  args.q_blocks = (d.rows + ATT_CTA_ROWS - 1) / ATT_CTA_ROWS;
+  args.num_units = static_cast<int>(std::min<long long>(
+      static_cast<long long>(args.q_blocks) * d.heads_q * d.batch, 0x7fffffffLL));
   args.scale_log2 = p->scale * 1.4426950408889634f;
   args.O = static_cast<__half*>(O);
   args.lse = lse;
   args.status = status;
   args.timeout_ns = wait_timeout_ns();
 
-  if (d.head_dim == 128) return launch_forward<128>(tq, tk, tv, args, d, st, duplicated_count);
-  return launch_forward<64>(tq, tk, tv, args, d, st, duplicated_count);
+  if (d.head_dim == 128) return launch_forward<128>(tq, tk, tv, args, d, info.sm_count, st, duplicated_count);
+  return launch_forward<64>(tq, tk, tv, args, d, info.sm_count, st, duplicated_count);
 }
 
 template <int D>
