@@ -34,7 +34,10 @@
 //                                operand.
 // The next unit of a buffer overwrites those fp16 pairs, so its S / dP MMAs
 // are issued only after the commit of the MMAs that read them has completed
-// (buf_free[b], an mbarrier), never on the strength of issue order.
+// (buf_free[b], an mbarrier), never on the strength of issue order. Two
+// threads issue: warp 1 the S / dP MMAs (N = 64), warp 2 the accumulating
+// ones (N = D), each in unit order, so accumulation order is fixed and the
+// results are deterministic.
 //
 // TMEM columns (512), dK/dV kernel: [0,128) buffer 0 | [128,256) buffer 1 |
 // [256,256+D) dV | [256+D,256+2D) dK. dQ kernel: [0,128) buffer 0 |
@@ -59,7 +62,7 @@ struct AttnBwdArgs {
   unsigned long long timeout_ns;
 };
 
-constexpr int ATB_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4-7 / 8-11 element-wise (buffer 0 / 1)
+constexpr int ATB_THREADS = 384;  // warp 0 TMA, warps 1-2 MMA, warps 4-7 / 8-11 element-wise (buffer 0 / 1)
 constexpr int ATB_STAGES = 2;
 // Of every 8 exponentials of the element-wise step, this many (an even
 // number) take the FMA-pipe cubic ex2_poly2 and the rest MUFU.
@@ -127,54 +130,55 @@ __global__ void __launch_bounds__(256) attention_bwd_prep_kernel(const __half* _
   }
 }
 
-// One unit of a thread's S / dP row pair (64 columns, two steps of 32):
-// P = 2^(s * scale_log2 - lse2), dS = P * (dP - D) * scale. Column c (0..63
-// of the unit) uses lse2_of(c) / d_of(c) and is zeroed when !valid(c). After
-// each step its fp16 pairs are stored: with want_p, P over the S columns and
-// dS over the dP columns (the dK/dV kernel reads both); without, dS over the
-// S columns (the dQ kernel reads only dS). A step overwrites only columns an
-// earlier step (or itself) has already read.
-template <typename LseF, typename DF, typename ValidF>
-__device__ __forceinline__ void atb_elementwise_unit(uint32_t tS, uint32_t tP, float sl2, float scale, LseF lse2_of,
-                                                     DF d_of, ValidF valid, bool want_p) {
+// The element-wise step of one unit is split by columns between the two
+// element-wise warpgroups: warpgroup w takes columns [32 w, 32 w + 32) of the
+// unit's S (or S^T) and dP (or dP^T), and writes its fp16 pairs over the
+// first 16 of those columns, which it alone reads. The accumulating MMAs
+// find their A operand (K = 64) at column offsets 0, 8, 32, 40.
+//
+// P for the 32 columns at c0 of this thread's S row: 2^(s * sl2 - lse2),
+// zero where !valid(c). ATB_EMU_PER8 of every 8 exponentials on the FMA pipe.
+template <typename LseF, typename ValidF>
+__device__ __forceinline__ void atb_p32(uint32_t tS, int c0, float sl2, LseF lse2_of, ValidF valid,
+                                        float2 (&p)[16]) {
+  uint32_t vs[32];
+  tmem_ld_32x32b_x32(tS + c0, vs);
+  tmem_ld_wait();
+  const float2 sc = make_float2(sl2, sl2);
 #pragma unroll
-  for (int sub = 0; sub < 2; ++sub) {
-    const int c0 = sub * 32;
-    uint32_t vs[32], vp[32];
-    tmem_ld_32x32b_x32(tS + c0, vs);
-    tmem_ld_32x32b_x32(tP + c0, vp);
-    tmem_ld_wait();
-    uint32_t pp[16], pd[16];
-    const float2 sc = make_float2(sl2, sl2);
-    const float2 ds = make_float2(scale, scale);
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int c = c0 + 2 * e;
-      // exponent pair in one packed FMA; ATB_EMU_PER8 of every 8 exponentials on the FMA pipe
-      const float2 a = ffma2(make_float2(__uint_as_float(vs[2 * e]), __uint_as_float(vs[2 * e + 1])), sc,
-                             make_float2(-lse2_of(c), -lse2_of(c + 1)));
-      float2 pv;
-      if ((e & 3) * 2 >= 8 - ATB_EMU_PER8) {
-        pv = ex2_poly2(a);
-      } else {
-        pv.x = ex2_approx(a.x);
-        pv.y = ex2_approx(a.y);
-      }
-      if (!valid(c)) pv.x = 0.f;
-      if (!valid(c + 1)) pv.y = 0.f;
-      // dS = P * (dP - D) * scale = P * (dP * scale - D * scale)
-      const float2 t = ffma2(make_float2(__uint_as_float(vp[2 * e]), __uint_as_float(vp[2 * e + 1])), ds,
-                             make_float2(-d_of(c) * scale, -d_of(c + 1) * scale));
-      const float2 dv = ffma2(pv, t, make_float2(0.f, 0.f));
-      pp[e] = pack_half2(pv.x, pv.y);
-      pd[e] = pack_half2(dv.x, dv.y);
-    }
-    if (want_p) {
-      tmem_st_32x32b_x16(tS + sub * 16, pp);
-      tmem_st_32x32b_x16(tP + sub * 16, pd);
+  for (int e = 0; e < 16; ++e) {
+    const int c = c0 + 2 * e;
+    const float2 a = ffma2(make_float2(__uint_as_float(vs[2 * e]), __uint_as_float(vs[2 * e + 1])), sc,
+                           make_float2(-lse2_of(c), -lse2_of(c + 1)));
+    float2 pv;
+    if ((e & 3) * 2 >= 8 - ATB_EMU_PER8) {
+      pv = ex2_poly2(a);
     } else {
-      tmem_st_32x32b_x16(tS + sub * 16, pd);
+      pv.x = ex2_approx(a.x);
+      pv.y = ex2_approx(a.y);
     }
+    if (!valid(c)) pv.x = 0.f;
+    if (!valid(c + 1)) pv.y = 0.f;
+    p[e] = pv;
+  }
+}
+
+// dS = P * (dP - D) * scale = P * (dP * scale - D * scale) for the same 32
+// columns, read from this thread's dP row at tdP + c0; fp16 pairs out.
+template <typename DF>
+__device__ __forceinline__ void atb_ds32(uint32_t tdP, int c0, float scale, DF d_of, const float2 (&p)[16],
+                                         uint32_t (&pd)[16]) {
+  uint32_t vp[32];
+  tmem_ld_32x32b_x32(tdP + c0, vp);
+  tmem_ld_wait();
+  const float2 ds = make_float2(scale, scale);
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int c = c0 + 2 * e;
+    const float2 t = ffma2(make_float2(__uint_as_float(vp[2 * e]), __uint_as_float(vp[2 * e + 1])), ds,
+                           make_float2(-d_of(c) * scale, -d_of(c + 1) * scale));
+    const float2 dv = ffma2(p[e], t, make_float2(0.f, 0.f));
+    pd[e] = pack_half2(dv.x, dv.y);
   }
 }
 
@@ -219,16 +223,17 @@ __device__ __forceinline__ void atb_mma_nt_unit(uint32_t d_tmem, uint32_t a_addr
 }
 
 // Accumulating MMA of one unit (M = 128, N = D, K = 64): D[tmem] (+)=
-// A[tmem, fp16 pairs in 32 columns] * B, B the unit's 64 rows of a
-// [rows][D] tile read MN-major (`b_addr` at the unit's first row).
+// A[tmem, fp16 pairs at column offsets 0, 8, 32, 40 (see atb_p32)] * B, B
+// the unit's 64 rows of a [rows][D] tile read MN-major (`b_addr` at the
+// unit's first row).
 template <int D>
 __device__ __forceinline__ void atb_mma_tn_unit(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, bool acc) {
   constexpr uint32_t IDESC = idesc_f16_f32(ATT_BM, D, false, true);
   const uint64_t db = sw128_desc(b_addr, 16384, 1024);
 #pragma unroll
   for (int kk = 0; kk < ATT_BN / 32; ++kk)
-    umma_f16_ts(d_tmem, a_tmem + kk * 8, db + static_cast<uint32_t>(kk * (2048 >> 4)), IDESC,
-                (acc || kk > 0) ? 1u : 0u);
+    umma_f16_ts(d_tmem, a_tmem + (kk >> 1) * 32 + (kk & 1) * 8, db + static_cast<uint32_t>(kk * (2048 >> 4)),
+                IDESC, (acc || kk > 0) ? 1u : 0u);
 }
 
 template <int D>
@@ -250,10 +255,13 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;                 // STAGES
   uint64_t* q_empty = q_full + ATB_STAGES;     // STAGES
-  uint64_t* s_full = q_empty + ATB_STAGES;     // 2: a unit's S^T, dP^T in buffer b
-  uint64_t* p_full = s_full + 2;               // 2: its P^T, dS^T in buffer b
-  uint64_t* buf_free = p_full + 2;             // 2: the MMAs reading buffer b's P^T, dS^T completed
-  uint64_t* acc_full = buf_free + 2;           // dK, dV complete
+  uint64_t* s_full = q_empty + ATB_STAGES;     // 2: a unit's S^T in buffer b
+  uint64_t* dp_full = s_full + 2;              // 2: its dP^T
+  uint64_t* p_full = dp_full + 2;              // 2: its P^T (both element-wise warpgroups)
+  uint64_t* ds_full = p_full + 2;              // 2: its dS^T
+  uint64_t* free_s = ds_full + 2;              // 2: dV += P^T dO read buffer b's P^T
+  uint64_t* free_dp = free_s + 2;              // 2: dK += dS^T Q read its dS^T
+  uint64_t* acc_full = free_dp + 2;            // dK, dV complete
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -276,11 +284,14 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], ATT_BM);
-      mbar_init(&buf_free[i], 1);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&p_full[i], 2 * ATT_BM);
+      mbar_init(&ds_full[i], 2 * ATT_BM);
+      mbar_init(&free_s[i], 1);
+      mbar_init(&free_dp[i], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -320,72 +331,91 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       for (int n = (issued > ATB_STAGES ? issued - ATB_STAGES : 0); n < issued; ++n)
         mbar_wait(&q_full[n % ATB_STAGES], (n / ATB_STAGES) & 1, wd, SITE_ATB_PRODUCER_DRAIN);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 1 issues every unit's S^T, dP^T (N = 64), warp 2 the accumulating
+    // dV, dK MMAs (N = D) in unit order: one thread issues about one
+    // tcgen05.mma per 55 SM clocks, too few for the unit's 24 MMAs. Each
+    // half of a buffer is handed back separately: S^T of unit u + 2 follows
+    // dV += P^T dO of unit u, dP^T follows dK += dS^T Q.
     if (elect_one()) {
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      // S^T, dP^T of unit u into buffer u & 1 (its Q / dO stage must have landed).
-      auto issue_sdp = [&](int u) -> bool {
-        const int n = u >> 1, hf = u & 1, s = n % ATB_STAGES;
-        if (hf == 0 && !mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) return false;
-        tc_fence_after();
-        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 query rows
-        const uint32_t buf = tmem_base + hf * 128;
-        atb_mma_nt_unit<D>(buf, k_addr, smem_u32(sQ + s * TB) + rows);        // S^T = K_j Q^T
-        atb_mma_nt_unit<D>(buf + 64, v_addr, smem_u32(sdO + s * TB) + rows);  // dP^T = V_j dO^T
-        umma_commit(&s_full[hf]);
-        return true;
-      };
       bool ok = mbar_wait(kv_full, 0, wd, SITE_ATB_MMA_FIXED);
-      if (ok) ok = issue_sdp(0);
-      if (ok && units > 1) ok = issue_sdp(1);
       for (int u = 0; u < units && ok; ++u) {
         const int n = u >> 1, hf = u & 1, s = n % ATB_STAGES;
-        const uint32_t par = static_cast<uint32_t>(n & 1);
-        if (!mbar_wait(&p_full[hf], par, wd, SITE_ATB_MMA_P)) break;
-        tc_fence_after();
-        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;
+        const uint32_t par = static_cast<uint32_t>(n & 1), prev = par ^ 1u;
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 query rows
         const uint32_t buf = tmem_base + hf * 128;
-        atb_mma_tn_unit<D>(tmem_base + 256, buf, smem_u32(sdO + s * TB) + rows, u > 0);      // dV += P^T dO
-        atb_mma_tn_unit<D>(tmem_base + 256 + D, buf + 64, smem_u32(sQ + s * TB) + rows, u > 0);  // dK += dS^T Q
-        umma_commit(&buf_free[hf]);
-        if (hf == 1) umma_commit(&q_empty[s]);
-        if (u + 2 < units) {
-          // Unit u + 2 reuses this buffer: its S^T overwrites the P^T just read.
-          if (!mbar_wait(&buf_free[hf], par, wd, SITE_ATB_MMA_FREE)) break;
-          ok = issue_sdp(u + 2);
+        if (warp == 1) {
+          if (hf == 0 && !mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+          if (u >= 2 && !mbar_wait(&free_s[hf], prev, wd, SITE_ATB_MMA_FREE)) break;
+          tc_fence_after();
+          atb_mma_nt_unit<D>(buf, k_addr, smem_u32(sQ + s * TB) + rows);  // S^T = K_j Q^T
+          umma_commit(&s_full[hf]);
+          if (u >= 2 && !mbar_wait(&free_dp[hf], prev, wd, SITE_ATB_MMA_FREE)) break;
+          tc_fence_after();
+          atb_mma_nt_unit<D>(buf + 64, v_addr, smem_u32(sdO + s * TB) + rows);  // dP^T = V_j dO^T
+          umma_commit(&dp_full[hf]);
+        } else {
+          if (hf == 0 && !mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+          if (!mbar_wait(&p_full[hf], par, wd, SITE_ATB_MMA_P)) break;
+          tc_fence_after();
+          atb_mma_tn_unit<D>(tmem_base + 256, buf, smem_u32(sdO + s * TB) + rows, u > 0);  // dV += P^T dO
+          umma_commit(&free_s[hf]);
+          if (!mbar_wait(&ds_full[hf], par, wd, SITE_ATB_MMA_P)) break;
+          tc_fence_after();
+          atb_mma_tn_unit<D>(tmem_base + 256 + D, buf + 64, smem_u32(sQ + s * TB) + rows, u > 0);  // dK += dS^T Q
+          umma_commit(&free_dp[hf]);
+          if (hf == 1) umma_commit(&q_empty[s]);
         }
       }
-      umma_commit(acc_full);
+      if (warp == 2) umma_commit(acc_full);
       umma_commit(drain);
       mbar_wait(drain, 0, wd, SITE_ATB_MMA_DRAIN);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ P^T, dS^T and the epilogue
-    const int hf = (warp - 4) >> 2;  // buffer (query half) of this warpgroup
+    // Both warpgroups work on every unit, warpgroup w on its columns
+    // [32 w, 32 w + 32) (query rows of the unit); P^T is released first so
+    // dV += P^T dO can start while dS^T is formed.
+    const int w = (warp - 4) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;    // key row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t tS = tmem_base + hf * 128 + lane_off;
-    const uint32_t tP = tS + 64;
+    const int c0 = 32 * w;
     bool ok = true;
-    for (int n = 0; n < iters; ++n) {
-      const int s = n % ATB_STAGES;
+    for (int u = 0; u < units; ++u) {
+      const int n = u >> 1, hf = u & 1, s = n % ATB_STAGES;
+      const uint32_t tS = tmem_base + hf * 128 + lane_off;
       // The stage's LSE / D vectors arrive by bulk copy on q_full[s]; waiting
       // on that phase too makes them visible here. It cannot have moved on:
-      // the stage is refilled only after this unit's p_full.
+      // the stage is refilled only after this tile's last dS^T is consumed.
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hf], n & 1, wd, SITE_ATB_EW_S) &&
                                        mbar_wait(&q_full[s], (n / ATB_STAGES) & 1, wd, SITE_ATB_EW_S));
       if (!ok) break;
       tc_fence_after();
       const float* L = sL + s * ATT_BM + hf * 64;
       const float* Dv = sD + s * ATT_BM + hf * 64;
-      atb_elementwise_unit(
-          tS, tP, args.scale_log2, args.scale, [&](int c) { return L[c]; }, [&](int c) { return Dv[c]; },
-          [](int) { return true; }, true);
+      float2 p[16];
+      atb_p32(tS, c0, args.scale_log2, [&](int c) { return L[c]; }, [](int) { return true; }, p);
+      {
+        uint32_t pp[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pp[e] = pack_half2(p[e].x, p[e].y);
+        tmem_st_32x32b_x16(tS + c0, pp);
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[hf]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&dp_full[hf], n & 1, wd, SITE_ATB_EW_S));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t pd[16];
+      atb_ds32(tS + 64, c0, args.scale, [&](int c) { return Dv[c]; }, p, pd);
+      tmem_st_32x32b_x16(tS + 64 + c0, pd);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&ds_full[hf]);
     }
     if (ok && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
       tc_fence_after();
@@ -393,7 +423,7 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       const bool live = row < args.C;
       const long long off = attn_row_offset(args.layout, b, args.heads_kv, args.C, hk, live ? row : 0, D);
       // warpgroup 0 stores dV, warpgroup 1 dK
-      if (hf == 0)
+      if (w == 0)
         atb_store_row<D>(tmem_base + 256 + lane_off, live ? args.dV + off : nullptr);
       else
         atb_store_row<D>(tmem_base + 256 + D + lane_off, live ? args.dK + off : nullptr);
@@ -425,9 +455,10 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;                // STAGES
   uint64_t* kv_empty = kv_full + ATB_STAGES;   // STAGES
-  uint64_t* s_full = kv_empty + ATB_STAGES;    // 2
-  uint64_t* p_full = s_full + 2;               // 2
-  uint64_t* buf_free = p_full + 2;             // 2
+  uint64_t* s_full = kv_empty + ATB_STAGES;    // 2: a unit's S in buffer b
+  uint64_t* dp_full = s_full + 2;              // 2: its dP
+  uint64_t* ds_full = dp_full + 2;             // 2: its dS (both element-wise warpgroups)
+  uint64_t* buf_free = ds_full + 2;            // 2: dQ += dS K read buffer b's dS
   uint64_t* acc_full = buf_free + 2;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -450,11 +481,12 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], ATT_BM);
+      mbar_init(&dp_full[i], 1);
+      mbar_init(&ds_full[i], 2 * ATT_BM);
       mbar_init(&buf_free[i], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -489,70 +521,74 @@ __global__ void __launch_bounds__(ATB_THREADS, 1)
       for (int j = (issued > ATB_STAGES ? issued - ATB_STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % ATB_STAGES], (j / ATB_STAGES) & 1, wd, SITE_ATB_PRODUCER_DRAIN);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 1 issues every unit's S, dP (N = 64), warp 2 the accumulating dQ
+    // MMAs (N = D) in unit order.
     if (elect_one()) {
       const uint32_t q_addr = smem_u32(sQ), g_addr = smem_u32(sdO);
-      // S, dP of unit u (keys of half u & 1 of tile u >> 1) into buffer u & 1.
-      auto issue_sdp = [&](int u) -> bool {
-        const int j = u >> 1, hf = u & 1, s = j % ATB_STAGES;
-        if (hf == 0 && !mbar_wait(&kv_full[s], (j / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) return false;
-        tc_fence_after();
-        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 key rows
-        const uint32_t buf = tmem_base + hf * 128;
-        atb_mma_nt_unit<D>(buf, q_addr, smem_u32(sK + s * TB) + rows);       // S = Q_i K^T
-        atb_mma_nt_unit<D>(buf + 64, g_addr, smem_u32(sV + s * TB) + rows);  // dP = dO_i V^T
-        umma_commit(&s_full[hf]);
-        return true;
-      };
       bool ok = mbar_wait(q_full, 0, wd, SITE_ATB_MMA_FIXED);
-      if (ok) ok = issue_sdp(0);
-      if (ok && units > 1) ok = issue_sdp(1);
       for (int u = 0; u < units && ok; ++u) {
         const int j = u >> 1, hf = u & 1, s = j % ATB_STAGES;
-        const uint32_t par = static_cast<uint32_t>(j & 1);
-        if (!mbar_wait(&p_full[hf], par, wd, SITE_ATB_MMA_P)) break;
-        tc_fence_after();
-        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;
-        atb_mma_tn_unit<D>(tmem_base + 256, tmem_base + hf * 128, smem_u32(sK + s * TB) + rows,
-                        u > 0);  // dQ += dS K
-        umma_commit(&buf_free[hf]);
-        if (hf == 1) umma_commit(&kv_empty[s]);
-        if (u + 2 < units) {
-          if (!mbar_wait(&buf_free[hf], par, wd, SITE_ATB_MMA_FREE)) break;
-          ok = issue_sdp(u + 2);
+        const uint32_t rows = static_cast<uint32_t>(hf) * 8192u;  // the unit's 64 key rows
+        const uint32_t buf = tmem_base + hf * 128;
+        if (warp == 1) {
+          // Unit u reuses buffer hf: its S overwrites the dS unit u - 2's dQ
+          // MMAs read.
+          if (u >= 2 && !mbar_wait(&buf_free[hf], ((u - 2) >> 1) & 1, wd, SITE_ATB_MMA_FREE)) break;
+          if (hf == 0 && !mbar_wait(&kv_full[s], (j / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+          tc_fence_after();
+          atb_mma_nt_unit<D>(buf, q_addr, smem_u32(sK + s * TB) + rows);  // S = Q_i K^T
+          umma_commit(&s_full[hf]);
+          atb_mma_nt_unit<D>(buf + 64, g_addr, smem_u32(sV + s * TB) + rows);  // dP = dO_i V^T
+          umma_commit(&dp_full[hf]);
+        } else {
+          if (!mbar_wait(&ds_full[hf], j & 1, wd, SITE_ATB_MMA_P)) break;
+          if (hf == 0 && !mbar_wait(&kv_full[s], (j / ATB_STAGES) & 1, wd, SITE_ATB_MMA_STREAM)) break;
+          tc_fence_after();
+          atb_mma_tn_unit<D>(tmem_base + 256, buf, smem_u32(sK + s * TB) + rows, u > 0);  // dQ += dS K
+          umma_commit(&buf_free[hf]);
+          if (hf == 1) umma_commit(&kv_empty[s]);
         }
       }
-      umma_commit(acc_full);
+      if (warp == 2) umma_commit(acc_full);
       umma_commit(drain);
       mbar_wait(drain, 0, wd, SITE_ATB_MMA_DRAIN);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ dS and the epilogue
-    const int hf = (warp - 4) >> 2;  // buffer (key half) of this warpgroup
+    // Both warpgroups work on every unit, warpgroup w on its columns
+    // [32 w, 32 w + 32) (keys of the unit); P stays in registers.
+    const int w = (warp - 4) >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;    // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(qd * 32) << 16;
-    const uint32_t tS = tmem_base + hf * 128 + lane_off;
-    const uint32_t tP = tS + 64;
+    const int c0 = 32 * w;
     const long long voff = (static_cast<long long>(b) * args.heads_q + h) * args.R_pad + q0 + r;
     const float lse2 = args.lse2[voff];
     const float dterm = args.dvec[voff];
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
+    for (int u = 0; u < units; ++u) {
+      const int j = u >> 1, hf = u & 1;
+      const uint32_t tS = tmem_base + hf * 128 + lane_off;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hf], j & 1, wd, SITE_ATB_EW_S));
       if (!ok) break;
       tc_fence_after();
       const int valid = args.C - j * ATT_BN - hf * 64;  // key columns of this unit inside C
-      // dS over S (the MMA reads dS from the S columns); P is not needed here.
-      atb_elementwise_unit(
-          tS, tP, args.scale_log2, args.scale, [&](int) { return lse2; }, [&](int) { return dterm; },
-          [&](int c) { return c < valid; }, false);
+      float2 p[16];
+      atb_p32(tS, c0, args.scale_log2, [&](int) { return lse2; }, [&](int c) { return c < valid; }, p);
+      ok = __all_sync(0xffffffffu, mbar_wait(&dp_full[hf], j & 1, wd, SITE_ATB_EW_S));
+      if (!ok) break;
+      tc_fence_after();
+      // dS over this warpgroup's S columns (the dQ MMA reads it there).
+      uint32_t pd[16];
+      atb_ds32(tS + 64, c0, args.scale, [&](int) { return dterm; }, p, pd);
+      tmem_st_32x32b_x16(tS + c0, pd);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[hf]);
+      mbar_arrive(&ds_full[hf]);
     }
-    if (ok && hf == 0 && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
+    if (ok && w == 0 && __all_sync(0xffffffffu, mbar_wait(acc_full, 0, wd, SITE_ATB_EW_ACC))) {
       tc_fence_after();
       const int row = q0 + r;
       const bool live = row < args.R;
