@@ -154,10 +154,16 @@ def check(status: int) -> None:
 
 
 def stream_handle(stream=None) -> int | None:
-    """cudaStream_t of a torch stream (default: torch's current stream)."""
+    """cudaStream_t of a torch stream (default: torch's current stream on the current device). The default
+    is read through torch's raw-stream query, which skips building a Stream object (~0.3 us against ~3 us
+    per call)."""
     import torch
-    s = torch.cuda.current_stream() if stream is None else stream
-    return s.cuda_stream or None
+    if stream is None:
+        raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+        if raw is not None:
+            return raw(torch._C._cuda_getDevice()) or None
+        stream = torch.cuda.current_stream()
+    return stream.cuda_stream or None
 
 
 def sync_check(stream=None) -> None:
