@@ -15,12 +15,13 @@
 //               rings (128-byte-swizzled boxes of 64 columns x 128 rows).
 //   warp 1      TMEM alloc (512 columns: two 64-column S slots per Q tile,
 //               then O0 | O1).
-//   warps 1, 2  one elected lane each issues Q tile 0's / 1's tcgen05.mma.
+//   warps 1, 2  one elected lane each issues tcgen05.mma: at D = 128 warp 1
+//               every S and warp 2 every P.V, at D = 64 one warp per Q tile.
 //               S_i(n) = Q_i K(n)^T (M=128, N=64, both operands in smem) goes
 //               to slot n % 2 of tile i; O_i += P_i(n) V(n) (M=128, N=D,
 //               K=64) reads P_i(n) from TMEM and V as an MN-major smem
-//               operand. Per step n: PV_i(n), then S_i(n+2): S runs two steps
-//               ahead of the softmax.
+//               operand. S_i(n+2) follows PV_i(n): S runs two steps ahead of
+//               the softmax.
 //   warps 4-7   softmax of Q tile 0, warps 8-11 of Q tile 1: thread r owns
 //               query row r (TMEM lane r). Per step it reads its 64 scores
 //               (tcgen05.ld), forms P = 2^(s - m) against the running max m
@@ -127,6 +128,11 @@ struct AttFwdCfg {
   // moving 2 of 8 off MUFU pays (B4 H16 S4096 on one B200: D = 128 0.449 ms
   // with 0, 0.464 with 2; D = 64 0.360 ms with 2, 0.374 with 0).
   static constexpr int EMU_PER8 = (D == 128) ? 0 : 2;
+  // How the two MMA-issuing warps share the work. D = 128: warp 1 issues
+  // every S MMA and warp 2 every P.V MMA, so a P.V is never queued behind
+  // the issue of the other kind (0.441 ms against 0.452 ms per Q tile). D = 64:
+  // one warp per Q tile (0.360 ms against 0.363).
+  static constexpr bool ISSUE_BY_KIND = (D == 128);
 };
 
 // Loads one 128-row tile of head dim D (D/64 boxes of 64 columns).
@@ -281,11 +287,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(drain, 2);
     for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 2);
+      mbar_init(&k_empty[i], Cfg::ISSUE_BY_KIND ? 1 : 2);
     }
     for (int i = 0; i < VS; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 2);
+      mbar_init(&v_empty[i], Cfg::ISSUE_BY_KIND ? 1 : 2);
     }
     fence_mbar_init();
   }
@@ -355,11 +361,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   } else if (warp == 1 || warp == 2) {
     // ---------------------------------------------------------- MMA issuers
-    // Warp 1 issues Q tile 0's MMAs, warp 2 Q tile 1's: one thread issues
-    // about one tcgen05.mma per 55 SM clocks, so a single issuer could not
-    // keep the tensor core fed with N = 64 S MMAs.
+    // Two issuing warps (Cfg::ISSUE_BY_KIND: all S / all P.V, else one per
+    // Q tile): one thread issues about one tcgen05.mma per 55 SM clocks, so
+    // a single issuer could not keep the tensor core fed with N = 64 S MMAs.
     if (elect_one()) {
-      const int i = warp - 1;
       // Shared-memory descriptors of the tile bases; a descriptor's low 14
       // bits hold (address >> 4), so the offsets inside a tile are added to
       // it directly (every address stays below 256 KB).
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         umma_commit(&s_full[2 * i + (g & 1)]);
         if (n == nst - 1) umma_commit(&q_empty[i]);
-        if (last_step_of_tile(n)) umma_commit(&k_empty[ks]);
+        if ((!Cfg::ISSUE_BY_KIND || i == 1) && last_step_of_tile(n)) umma_commit(&k_empty[ks]);
         return true;
       };
       // O_i += P_i(g) V(g): P_i(g) is fp16 pairs in the first 32 columns of
@@ -427,21 +432,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                       (n > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&pv_done[2 * i + (g & 1)]);
         if (n == nst - 1) umma_commit(&o_full[i]);
-        if (last_step_of_tile(n)) umma_commit(&v_empty[vs]);
+        if ((!Cfg::ISSUE_BY_KIND || i == 1) && last_step_of_tile(n)) umma_commit(&v_empty[vs]);
         return true;
       };
       const Pos first{0, 0, 0, 0};
       Pos second = first;
       advance(second);
-      bool ok = do_s(i, first) && (total < 2 || do_s(i, second));
-      // Per step g: this tile's P.V, then S_i(g + 2) into the slot that P.V
-      // frees. While this issuer waits for the P.V to complete, the other
-      // tile's issuer keeps the tensor core busy.
-      Pos pv = first, sx = second;
-      advance(sx);
-      for (; pv.g < total && ok; advance(pv), advance(sx)) {
-        ok = do_pv(i, pv);
-        if (ok && sx.g < total) ok = do_s(i, sx);
+      bool ok = true;
+      if constexpr (Cfg::ISSUE_BY_KIND) {
+        // Warp 1: S_0(g), S_1(g) for every step, each into the slot its P.V
+        // of step g - 2 frees. Warp 2: P.V_0(g), P.V_1(g) as the P arrive.
+        if (warp == 1) {
+          ok = do_s(0, first) && (total < 2 || do_s(0, second)) && do_s(1, first) &&
+               (total < 2 || do_s(1, second));
+          Pos sx = second;
+          for (advance(sx); sx.g < total && ok; advance(sx)) ok = do_s(0, sx) && do_s(1, sx);
+        } else {
+          for (Pos pv = first; pv.g < total && ok; advance(pv)) ok = do_pv(0, pv) && do_pv(1, pv);
+        }
+      } else {
+        // Per step g: this tile's P.V, then S_i(g + 2) into the slot that
+        // P.V frees. While this issuer waits for the P.V to complete, the
+        // other tile's issuer keeps the tensor core busy.
+        const int i = warp - 1;
+        ok = do_s(i, first) && (total < 2 || do_s(i, second));
+        Pos pv = first, sx = second;
+        advance(sx);
+        for (; pv.g < total && ok; advance(pv), advance(sx)) {
+          ok = do_pv(i, pv);
+          if (ok && sx.g < total) ok = do_s(i, sx);
+        }
       }
       umma_commit(drain);
       mbar_wait(drain, 0, wd, SITE_ATT_MMA_DRAIN);
