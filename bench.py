@@ -570,11 +570,9 @@ def build_attention(w, dist, dev, gen, l2):
     hO = torch.empty(O.shape, dtype=O.dtype).pin_memory()
 
     def e2e_step():
-        Q.copy_(hQ, non_blocking=True)
-        K.copy_(hK, non_blocking=True)
-        V.copy_(hV, non_blocking=True)
-        plan.run(Q, K, V, O=O)
-        hO.copy_(O, non_blocking=True)
+        # Host buffers in and out through the host-buffer entry point: copies in, kernels and copies out
+        # pipelined over 16 chunks of (batch, head) units (mm4_attention_fwd_host).
+        plan.run_host(hQ, hK, hV, hO, (Q, K, V, O))
     return step, e2e_step, (3 * Q.numel() * 2, O.numel() * 2), plan.kernel_name, 1, "strong", sets
 
 

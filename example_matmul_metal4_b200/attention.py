@@ -106,6 +106,25 @@ class AttentionPlan:
                                              _lib.stream_handle(stream), int(duplicatedCount)))
         return O
 
+    def run_host(self, Q, K, V, O, staging, chunks: int = 16, stream=None):
+        """O = softmax(scale Q K^T) V for CPU tensors (pinned for the copies to overlap): Q, K, V are copied
+        in through the CUDA tensors `staging` = (dQ, dK, dV, dO) of the full shapes, and O is copied out,
+        as a pipeline over `chunks` pieces of the (batch, head) units (mm4_attention_fwd_host). Ordered on
+        `stream`; the result is in O once the stream reaches the end of the call."""
+        import torch
+        d = self.dims
+        dQ, dK, dV, dO = staging
+        self._check(Q=dQ, K=dK, V=dV, O=dO)
+        shapes = {"Q": self.shape(d.R, d.Hq), "K": self.shape(d.C, d.Hk), "V": self.shape(d.C, d.Hk),
+                  "O": self.shape(d.R, d.Hq)}
+        for n, t in (("Q", Q), ("K", K), ("V", V), ("O", O)):
+            if t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous() or tuple(t.shape) != shapes[n]:
+                raise ValueError(f"{n} must be a contiguous CPU fp16 tensor of shape {shapes[n]}")
+        _lib.check(self._L.mm4_attention_fwd_host(self._h, Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                                  dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), dO.data_ptr(),
+                                                  int(chunks), _lib.stream_handle(stream)))
+        return O
+
     def backward_workspace_bytes(self) -> int:
         """Bytes of scratch `backward` needs (any contents, 16-byte aligned)."""
         return int(self._L.mm4_attention_bwd_workspace_size(self._h))

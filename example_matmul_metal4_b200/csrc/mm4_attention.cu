@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "attention_bwd_sm100.cuh"
@@ -178,6 +179,35 @@ mm4_status launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const C
   return MM4_OK;
 }
 
+// Side streams and events of the host-buffer forward, created once per device.
+constexpr int kHostMaxChunks = 64;
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start, end, loaded[kHostMaxChunks], done[kHostMaxChunks];
+};
+constexpr int kHostMaxDevices = 64;
+HostPipe g_host_pipe[kHostMaxDevices];
+std::mutex g_host_mutex;
+
+mm4_status host_pipe(int dev, HostPipe** out) {
+  if (dev < 0 || dev >= kHostMaxDevices) return fail(MM4_ERR_CUDA, "device id %d out of range", dev);
+  HostPipe& hp = g_host_pipe[dev];
+  if (!hp.ready) {
+    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.in, cudaStreamNonBlocking));
+    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.out, cudaStreamNonBlocking));
+    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.start, cudaEventDisableTiming));
+    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.end, cudaEventDisableTiming));
+    for (int i = 0; i < kHostMaxChunks; ++i) {
+      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.loaded[i], cudaEventDisableTiming));
+      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.done[i], cudaEventDisableTiming));
+    }
+    hp.ready = true;
+  }
+  *out = &hp;
+  return MM4_OK;
+}
+
 int padded_rows(const mm4_attention_desc& d) { return (d.rows + ATT_BM - 1) / ATT_BM * ATT_BM; }
 
 size_t bwd_workspace_bytes(const mm4_attention_desc& d) {
@@ -197,6 +227,63 @@ mm4_status mm4_attention_fwd_lse(const mm4_attention_plan* p, const void* Q, con
                                  float* lse, mm4_stream_t stream) {
   if (!lse) return fail(MM4_ERR_INVALID, "null lse pointer");
   return attention_forward(p, Q, K, V, O, lse, static_cast<cudaStream_t>(stream), 1);
+}
+
+mm4_status mm4_attention_fwd_host(const mm4_attention_plan* p, const void* hQ, const void* hK, const void* hV,
+                                  void* hO, void* dQ, void* dK, void* dV, void* dO, int32_t chunks,
+                                  mm4_stream_t stream) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!hQ || !hK || !hV || !hO || !dQ || !dK || !dV || !dO) return fail(MM4_ERR_INVALID, "null buffer pointer");
+  const mm4_attention_desc& d = p->d;
+  const int group = d.heads_q / d.heads_kv;
+  // Pieces that a chunk may hold whole: a key/value head with its query heads
+  // ([B][H][S][D]), or a batch element ([B][S][H][D]).
+  const bool bhsd = d.layout == MM4_ATTN_BHSD;
+  const long long pieces = bhsd ? static_cast<long long>(d.batch) * d.heads_kv : d.batch;
+  const size_t elt = 2;
+  const size_t q_piece = (bhsd ? static_cast<size_t>(group) : static_cast<size_t>(d.heads_q)) * d.rows * d.head_dim * elt;
+  const size_t kv_piece = (bhsd ? 1 : static_cast<size_t>(d.heads_kv)) * d.columns * d.head_dim * elt;
+  int n = chunks > 0 ? chunks : 16;
+  n = static_cast<int>(std::min<long long>(std::min(n, kHostMaxChunks), pieces));
+  int dev = -1;
+  MM4_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_host_mutex);
+  HostPipe* hp = nullptr;
+  mm4_status rc = host_pipe(dev, &hp);
+  if (rc != MM4_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+  for (int c = 0; c < n; ++c) {
+    const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
+    const size_t qo = static_cast<size_t>(p0) * q_piece, qn = static_cast<size_t>(np) * q_piece;
+    const size_t ko = static_cast<size_t>(p0) * kv_piece, kn = static_cast<size_t>(np) * kv_piece;
+    MM4_CUDA_TRY(cudaMemcpyAsync(at(dQ, qo), at(hQ, qo), qn, cudaMemcpyHostToDevice, hp->in));
+    MM4_CUDA_TRY(cudaMemcpyAsync(at(dK, ko), at(hK, ko), kn, cudaMemcpyHostToDevice, hp->in));
+    MM4_CUDA_TRY(cudaMemcpyAsync(at(dV, ko), at(hV, ko), kn, cudaMemcpyHostToDevice, hp->in));
+    MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+    // The chunk as a problem of its own: its (batch, head) units are
+    // computed exactly as in the whole problem.
+    mm4_attention_plan sub = *p;
+    if (bhsd) {
+      sub.d.batch = 1;
+      sub.d.heads_q = static_cast<int32_t>(np * group);
+      sub.d.heads_kv = static_cast<int32_t>(np);
+    } else {
+      sub.d.batch = static_cast<int32_t>(np);
+    }
+    rc = attention_forward(&sub, at(dQ, qo), at(dK, ko), at(dV, ko), at(dO, qo), nullptr, st, 1);
+    if (rc != MM4_OK) return rc;
+    MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+    MM4_CUDA_TRY(cudaMemcpyAsync(at(hO, qo), at(dO, qo), qn, cudaMemcpyDeviceToHost, hp->out));
+  }
+  MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+  return MM4_OK;
 }
 
 size_t mm4_attention_bwd_workspace_size(const mm4_attention_plan* p) { return p ? bwd_workspace_bytes(p->d) : 0; }

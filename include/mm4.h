@@ -266,6 +266,23 @@ MM4_API mm4_status mm4_attention_fwd(const mm4_attention_plan* plan, const void*
 MM4_API mm4_status mm4_attention_fwd_lse(const mm4_attention_plan* plan, const void* Q, const void* K, const void* V,
                                          void* O, float* lse, mm4_stream_t stream);
 
+/* Forward from and to host memory: Q, K, V are read from hQ, hK, hV and O
+ * is written to hO (host buffers; page-locked for the copies to overlap),
+ * through the caller's device buffers dQ, dK, dV, dO of the plan's full
+ * sizes. The (batch, head) units are cut into `chunks` pieces (<= 0: 16; at
+ * most 64; whole key/value heads with their query heads in [B][H][S][D],
+ * whole batch elements in [B][S][H][D]) and run as a pipeline on `stream`
+ * and two library streams: copies in, the kernel, copies out, so the
+ * transfers in both directions overlap each other and the kernels. The
+ * reference's buffers are host-visible (Apple unified memory); this is the
+ * call for callers whose tensors live on the host. Ordered on `stream`:
+ * work queued on it before the call precedes the copies, and later work
+ * follows the last copy out. Results equal mm4_attention_fwd's bit for
+ * bit. */
+MM4_API mm4_status mm4_attention_fwd_host(const mm4_attention_plan* plan, const void* hQ, const void* hK,
+                                          const void* hV, void* hO, void* dQ, void* dK, void* dV, void* dO,
+                                          int32_t chunks, mm4_stream_t stream);
+
 /* Attention backward. The reference has it only as CPU code
  * (Network.swift:205-401: derivativeQ / derivativeK / derivativeV of the
  * loss sum(dO * O)); this is its GPU form. Inputs: Q, K, V, the forward's O

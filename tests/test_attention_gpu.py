@@ -126,3 +126,28 @@ def test_unsupported_head_dim_is_rejected():
     from example_matmul_metal4_b200 import MM4Error
     with pytest.raises(MM4Error):
         AttentionPlan(AttentionDimensions(64, 64, 96, 1, 1))
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("layout,B,Hq,Hk", [(MM4_ATTN_BHSD, 3, 4, 2), (MM4_ATTN_BSHD, 3, 4, 4)])
+def test_host_buffer_forward_matches_device_forward(cuda, D, layout, B, Hq, Hk):
+    """mm4_attention_fwd_host (pinned host Q, K, V in, O out; pipelined over chunks of whole key/value
+    heads or batch elements) gives the device forward's bits, for 1 chunk, a ragged split and more chunks
+    than pieces."""
+    import torch
+    R, C = 200, 333
+    plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
+    Q = _t(data.normal(plan.shape(R, Hq), 1.0, 5, 0), cuda)
+    K = _t(data.normal(plan.shape(C, Hk), 1.0, 5, 1), cuda)
+    V = _t(data.normal(plan.shape(C, Hk), 1.0, 5, 2), cuda)
+    ref = plan.run(Q, K, V)
+    sync_check()
+    ref = ref.cpu()
+    hQ, hK, hV = Q.cpu().pin_memory(), K.cpu().pin_memory(), V.cpu().pin_memory()
+    hO = torch.empty(ref.shape, dtype=torch.float16).pin_memory()
+    staging = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V), torch.empty_like(Q))
+    for chunks in (1, 4, 64):
+        hO.fill_(float("nan"))
+        plan.run_host(hQ, hK, hV, hO, staging, chunks=chunks)
+        sync_check()
+        assert torch.equal(hO, ref), chunks
