@@ -606,14 +606,13 @@ def build_attention_bwd(w, dist, dev, gen, l2):
 
     host = {k: v.cpu().pin_memory() for k, v in sets[0].items()}
     hout = [torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in (dQ, dK, dV)]
+    names = ("Q", "K", "V", "O", "dO", "lse")
 
     def e2e_step():
-        for k, v in sets[0].items():
-            v.copy_(host[k], non_blocking=True)
+        # Host buffers in and out through the host-buffer entry point (mm4_attention_bwd_host): copies in,
+        # the backward and copies out pipelined over 16 chunks of key/value heads.
         f = sets[0]
-        plan.backward(f["Q"], f["K"], f["V"], f["O"], f["dO"], f["lse"], dQ=dQ, dK=dK, dV=dV, workspace=ws)
-        for h, d in zip(hout, (dQ, dK, dV)):
-            h.copy_(d, non_blocking=True)
+        plan.backward_host(*(host[k] for k in names), *hout, tuple(f[k] for k in names), (dQ, dK, dV), ws)
     h2d = sum(v.numel() * v.element_size() for v in sets[0].values())
     d2h = 3 * Q.numel() * 2
     return (step, e2e_step, (h2d, d2h), "attention_bwd_sm100 (prep + dK/dV + dQ kernels)", 3, "strong",

@@ -109,6 +109,7 @@ SIGNATURES = {
     "mm4_attention_fwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int]),
     "mm4_attention_fwd_lse": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "mm4_attention_fwd_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp]),
+    "mm4_attention_bwd_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, ctypes.c_int32, _vp]),
     "mm4_attention_bwd_workspace_size": (_sz, [_vp]),
     "mm4_attention_bwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mm4_conv2d_plan_create": (ctypes.c_int, [ctypes.POINTER(_vp), ctypes.POINTER(Conv2dDesc)]),

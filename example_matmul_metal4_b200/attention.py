@@ -125,6 +125,29 @@ class AttentionPlan:
                                                   int(chunks), _lib.stream_handle(stream)))
         return O
 
+    def backward_host(self, Q, K, V, O, dO, lse, dQ, dK, dV, staging_in, staging_out, workspace, chunks: int = 16,
+                      stream=None):
+        """dQ, dK, dV (CPU fp16 outputs) of sum(dO * O) from CPU Q, K, V, O, dO (fp16) and lse (fp32), pinned
+        for the copies to overlap, through the CUDA tensors staging_in = (Q, K, V, O, dO, lse) and
+        staging_out = (dQ, dK, dV) of the full shapes: copies in, the backward and copies out run as a
+        pipeline over `chunks` pieces (mm4_attention_bwd_host). Ordered on `stream`."""
+        import torch
+        host_in, host_out = (Q, K, V, O, dO, lse), (dQ, dK, dV)
+        for t in host_in + host_out:
+            if t.is_cuda or not t.is_contiguous():
+                raise ValueError("host tensors must be contiguous CPU tensors")
+        for h, dv in zip(host_in + host_out, tuple(staging_in) + tuple(staging_out)):
+            if not dv.is_cuda or tuple(h.shape) != tuple(dv.shape) or h.dtype != dv.dtype or not dv.is_contiguous():
+                raise ValueError("staging tensors must be contiguous CUDA copies of the host tensors' shapes")
+        self._check(Q=staging_in[0], K=staging_in[1], V=staging_in[2], O=staging_in[3], dO=staging_in[4])
+        if tuple(lse.shape) != self.lse_shape() or lse.dtype != torch.float32:
+            raise ValueError(f"lse must be fp32 of shape {self.lse_shape()}")
+        arr = lambda ts: (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])  # noqa: E731
+        _lib.check(self._L.mm4_attention_bwd_host(self._h, arr(host_in), arr(host_out), arr(tuple(staging_in)),
+                                                  arr(tuple(staging_out)), workspace.data_ptr(), workspace.numel(),
+                                                  int(chunks), _lib.stream_handle(stream)))
+        return dQ, dK, dV
+
     def backward_workspace_bytes(self) -> int:
         """Bytes of scratch `backward` needs (any contents, 16-byte aligned)."""
         return int(self._L.mm4_attention_bwd_workspace_size(self._h))

@@ -341,6 +341,75 @@ mm4_status mm4_attention_bwd(const mm4_attention_plan* p, const void* Q, const v
   return launch_backward<64>(tq, tk, tv, tdo, args, d, O, dO, lse, st, info.sm_count);
 }
 
+mm4_status mm4_attention_bwd_host(const mm4_attention_plan* p, const void* const* host_in, void* const* host_out,
+                                  void* const* dev_in, void* const* dev_out, void* workspace, size_t workspace_bytes,
+                                  int32_t chunks, mm4_stream_t stream) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!host_in || !host_out || !dev_in || !dev_out) return fail(MM4_ERR_INVALID, "null buffer array");
+  for (int i = 0; i < 6; ++i)
+    if (!host_in[i] || !dev_in[i]) return fail(MM4_ERR_INVALID, "null input buffer %d", i);
+  for (int i = 0; i < 3; ++i)
+    if (!host_out[i] || !dev_out[i]) return fail(MM4_ERR_INVALID, "null output buffer %d", i);
+  const mm4_attention_desc& d = p->d;
+  const size_t need = bwd_workspace_bytes(d);
+  if (!workspace || workspace_bytes < need)
+    return fail(MM4_ERR_WORKSPACE, "attention backward needs a %zu-byte workspace", need);
+  const int group = d.heads_q / d.heads_kv;
+  const bool bhsd = d.layout == MM4_ATTN_BHSD;
+  const long long pieces = bhsd ? static_cast<long long>(d.batch) * d.heads_kv : d.batch;
+  const size_t qh = bhsd ? static_cast<size_t>(group) : static_cast<size_t>(d.heads_q);   // query heads per piece
+  const size_t kh = bhsd ? 1 : static_cast<size_t>(d.heads_kv);                           // key/value heads per piece
+  const size_t q_piece = qh * d.rows * d.head_dim * 2, kv_piece = kh * d.columns * d.head_dim * 2;
+  const size_t l_piece = qh * d.rows * sizeof(float);
+  const size_t w_piece = 2 * qh * padded_rows(d) * sizeof(float);
+  int n = chunks > 0 ? chunks : 16;
+  n = static_cast<int>(std::min<long long>(std::min(n, kHostMaxChunks), pieces));
+  int dev = -1;
+  MM4_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_host_mutex);
+  HostPipe* hp = nullptr;
+  mm4_status rc = host_pipe(dev, &hp);
+  if (rc != MM4_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+  for (int c = 0; c < n; ++c) {
+    const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
+    // Offsets and sizes of the chunk in Q / O / dO (and dQ), K / V (and dK, dV), lse.
+    const size_t qo = p0 * q_piece, qn = np * q_piece, ko = p0 * kv_piece, kn = np * kv_piece;
+    const size_t lo = p0 * l_piece, ln = np * l_piece;
+    const size_t in_off[6] = {qo, ko, ko, qo, qo, lo}, in_len[6] = {qn, kn, kn, qn, qn, ln};
+    for (int i = 0; i < 6; ++i)
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dev_in[i], in_off[i]), at(host_in[i], in_off[i]), in_len[i],
+                                   cudaMemcpyHostToDevice, hp->in));
+    MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+    mm4_attention_plan sub = *p;
+    if (bhsd) {
+      sub.d.batch = 1;
+      sub.d.heads_q = static_cast<int32_t>(np * group);
+      sub.d.heads_kv = static_cast<int32_t>(np);
+    } else {
+      sub.d.batch = static_cast<int32_t>(np);
+    }
+    rc = mm4_attention_bwd(&sub, at(dev_in[0], qo), at(dev_in[1], ko), at(dev_in[2], ko), at(dev_in[3], qo),
+                           at(dev_in[4], qo), reinterpret_cast<const float*>(at(dev_in[5], lo)), at(dev_out[0], qo),
+                           at(dev_out[1], ko), at(dev_out[2], ko), at(workspace, p0 * w_piece), np * w_piece, stream);
+    if (rc != MM4_OK) return rc;
+    MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+    const size_t out_off[3] = {qo, ko, ko}, out_len[3] = {qn, kn, kn};
+    for (int i = 0; i < 3; ++i)
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(host_out[i], out_off[i]), at(dev_out[i], out_off[i]), out_len[i],
+                                   cudaMemcpyDeviceToHost, hp->out));
+  }
+  MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+  MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+  return MM4_OK;
+}
+
 }  // extern "C"
 
 namespace {

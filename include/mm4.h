@@ -296,6 +296,18 @@ MM4_API mm4_status mm4_attention_bwd(const mm4_attention_plan* plan, const void*
                                      const void* O, const void* dO, const float* lse, void* dQ, void* dK, void* dV,
                                      void* workspace, size_t workspace_bytes, mm4_stream_t stream);
 
+/* Backward from and to host memory, as mm4_attention_fwd_host for the
+ * forward: host_in = {Q, K, V, O, dO, lse} and host_out = {dQ, dK, dV} are
+ * host buffers (page-locked for overlap); dev_in / dev_out the caller's
+ * device buffers of the same full sizes; workspace as for mm4_attention_bwd.
+ * Chunks of whole key/value heads (with their query heads, [B][H][S][D]) or
+ * batch elements ([B][S][H][D]) are copied in, differentiated and copied out
+ * as a pipeline. Results equal mm4_attention_bwd's bit for bit. */
+MM4_API mm4_status mm4_attention_bwd_host(const mm4_attention_plan* plan, const void* const* host_in,
+                                          void* const* host_out, void* const* dev_in, void* const* dev_out,
+                                          void* workspace, size_t workspace_bytes, int32_t chunks,
+                                          mm4_stream_t stream);
+
 /* ======================================================================== */
 /* Convolution (implicit GEMM)                                              */
 /* ======================================================================== */

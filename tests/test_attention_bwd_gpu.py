@@ -106,3 +106,34 @@ def test_backward_repeated_calls_are_bitwise_identical(cuda):
         sync_check()
         for a, b in zip(first, again):
             assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("layout,B,Hq,Hk", [(MM4_ATTN_BHSD, 3, 4, 2), (MM4_ATTN_BSHD, 3, 4, 4)])
+def test_host_buffer_backward_matches_device_backward(cuda, D, layout, B, Hq, Hk):
+    """mm4_attention_bwd_host (pinned host inputs and outputs, pipelined over chunks of key/value heads or
+    batch elements) gives mm4_attention_bwd's bits, for 1 chunk, a ragged split and more chunks than
+    pieces."""
+    import torch
+    R, C = 200, 333
+    plan = AttentionPlan(AttentionDimensions(R, C, D, Hq, Hk), batch=B, layout=layout)
+    Q = _t(data.normal(plan.shape(R, Hq), 1.0, 6, 0), cuda)
+    K = _t(data.normal(plan.shape(C, Hk), 1.0, 6, 1), cuda)
+    V = _t(data.normal(plan.shape(C, Hk), 1.0, 6, 2), cuda)
+    dO = _t(data.normal(plan.shape(R, Hq), 1.0, 6, 3), cuda)
+    lse = torch.empty(plan.lse_shape(), dtype=torch.float32, device=cuda)
+    O = plan.run(Q, K, V, lse=lse)
+    ws = torch.empty(plan.backward_workspace_bytes(), dtype=torch.uint8, device=cuda)
+    ref = [g.cpu() for g in plan.backward(Q, K, V, O, dO, lse, workspace=ws)]
+    sync_check()
+    host_in = tuple(x.cpu().pin_memory() for x in (Q, K, V, O, dO, lse))
+    host_out = tuple(torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in ref)
+    staging_in = tuple(torch.empty_like(x) for x in (Q, K, V, O, dO, lse))
+    staging_out = (torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V))
+    for chunks in (1, 4, 64):
+        for h in host_out:
+            h.fill_(float("nan"))
+        plan.backward_host(*host_in, *host_out, staging_in, staging_out, ws, chunks=chunks)
+        sync_check()
+        for name, h, r in zip(("dQ", "dK", "dV"), host_out, ref):
+            assert torch.equal(h, r), (chunks, name)
