@@ -135,6 +135,18 @@ struct AttFwdCfg {
   static constexpr bool ISSUE_BY_KIND = (D == 128);
 };
 
+// Prefetches one 128-row tile of head dim D into L2 (see att_load_tile_d).
+template <int D>
+__device__ __forceinline__ void att_prefetch_tile_d(const CUtensorMap* map, int layout, int row0, int head, int b) {
+#pragma unroll
+  for (int box = 0; box < D / 64; ++box) {
+    if (layout == 0)
+      tma_prefetch_l2_4d(map, box * 64, row0, head, b);
+    else
+      tma_prefetch_l2_4d(map, box * 64, head, row0, b);
+  }
+}
+
 // Loads one 128-row tile of head dim D (D/64 boxes of 64 columns).
 template <int D>
 __device__ __forceinline__ void att_load_tile_d(const CUtensorMap* map, uint64_t* bar, uint8_t* dst, int layout,
@@ -321,6 +333,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int hk = h / (args.heads_q / args.heads_kv);
         const int row0 = qb * ATT_CTA_ROWS;
         for (int j = 0; j < nkv && ok; ++j) {
+          // Halfway through a unit, bring the next unit's Q tiles and first
+          // K / V tiles into L2: their loads into shared memory can only
+          // start when this unit's last S MMAs free the buffers, and would
+          // otherwise wait the DRAM latency at the unit boundary.
+          if (j == nkv / 2 && ul + 1 < units) {
+            int nqb, nh, nb;
+            unit_of(ul + 1, nqb, nh, nb);
+            const int nhk = nh / (args.heads_q / args.heads_kv);
+            att_prefetch_tile_d<D>(&tmQ, args.layout, nqb * ATT_CTA_ROWS, nh, nb);
+            att_prefetch_tile_d<D>(&tmQ, args.layout, nqb * ATT_CTA_ROWS + ATT_BM, nh, nb);
+            att_prefetch_tile_d<D>(&tmK, args.layout, 0, nhk, nb);
+            att_prefetch_tile_d<D>(&tmV, args.layout, 0, nhk, nb);
+          }
           // Q_0 before the unit's first K tile, Q_1 after it; each waits for
           // the previous unit's last S_i.
           for (int i = 0; i < 2 && j == 0; ++i) {
