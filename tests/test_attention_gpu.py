@@ -151,3 +151,15 @@ def test_host_buffer_forward_matches_device_forward(cuda, D, layout, B, Hq, Hk):
         plan.run_host(hQ, hK, hV, hO, staging, chunks=chunks)
         sync_check()
         assert torch.equal(hO, ref), chunks
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_persistent_units_gqa_bshd_ragged(cuda, D):
+    """More (batch, head, 256-row) units than SMs with grouped-query heads, the [B][S][H][D] layout and
+    ragged rows and keys: every CTA of the persistent forward walks 2-3 units of different batches and
+    heads, each ending on a partial query block. Oracle rows at the start, across the first block edge and
+    at the end of R, for every (b, h)."""
+    B, Hq, Hk, R, C = 5, 16, 4, 1000, 777
+    for rows in ((0, 3), (254, 258), (997, 1000)):
+        plan, got, ref = _run(cuda, B, Hq, Hk, R, C, layout=MM4_ATTN_BSHD, rows=rows, D=D)
+        assert_close(got, ref, f"D={D} rows {rows}")
