@@ -43,23 +43,25 @@ enum GemmMode : int {
 // Multi-GPU split-K: each rank runs the same plan on its own K shard; the
 // ranks' fp32 partials meet in the epilogue over peer memory (one kernel per
 // GPU, no separate collective). The split-K scratch stays rank-local; each
-// rank publishes finished slices (a 128-row half tile x one split's row
-// range) into a staging area of its exchange buffer, which every other rank
-// maps. Per slice:
+// rank's exchange buffer holds two staging halves (by run parity) of one
+// slot per rank, and every other rank maps it. Per slice (a 128-row half
+// tile x one split's row range):
 //   1. on a rank that does not own the slice (the owner is the root, or
 //      slice % world in the spread mode), the CTA that completes the slice's
-//      rank-local sum copies the rows into its staging half for this run (two
-//      halves, by run parity), re-zeroes the scratch rows and raises
+//      rank-local sum pushes the rows into its own slot of the owner's
+//      staging half for this run (peer stores, posted over NVLink as soon as
+//      the rows are final), re-zeroes the scratch rows and raises
 //      ready[slice][rank] on the owner;
 //   2. the owner's CTA for the slice waits for the other ranks' flags, reads
-//      their rows from their staging (peer loads) and its own from its
-//      scratch, sums them in rank order, adds bias, rounds, stores the rows
-//      into the root's C (and raises done[slice] on the root when it is not
-//      the root itself); at its next launch it raises consumed[slice] on
+//      their rows from its own staging (local memory) and its own rows from
+//      its scratch, sums them in rank order, adds bias, rounds, stores the
+//      rows into the root's C (and raises done[slice] on the root when it is
+//      not the root itself); at its next launch it raises consumed[slice] on
 //      every rank;
-//   3. a rank overwrites a staging half (two runs later) only after the owner
-//      consumed it; the root's launch ends once every slice is in C.
-// Cross-GPU traffic is peer loads (and C stores) plus release/acquire flags
+//   3. a rank overwrites its slot of a staging half (two runs later) only
+//      after the owner consumed it; the root's launch ends once every slice
+//      is in C.
+// Cross-GPU traffic is peer stores (and C stores) plus release/acquire flags
 // that carry the run index + 1 (no remote atomics, nothing to reset).
 constexpr int MM4_MAX_GROUP = 8;
 struct SplitKGroupArgs {
@@ -68,7 +70,8 @@ struct SplitKGroupArgs {
   int owner_mode;                // 0: the root owns every slice; 1: slice % world (spread)
   int num_slices;                // half tiles x splits
   unsigned long long epoch;      // run index, the same on every rank
-  float* stage[MM4_MAX_GROUP];   // rank r's staging half for this run [rows][ws_ld] fp32 (peer-mapped)
+  float* stage[MM4_MAX_GROUP];   // rank r's staging half for this run: [world slots][rows][ws_ld] fp32 (peer-mapped)
+  long long slot_floats;         // floats per slot (one rank's partials)
   unsigned long long* ready[MM4_MAX_GROUP];     // rank r: [num_slices][world]
   unsigned long long* consumed[MM4_MAX_GROUP];  // rank r: [num_slices]
   unsigned long long* done;      // root: [num_slices]
@@ -193,12 +196,12 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
   const int tr = ethread / TPR;
   const int gc = col0 + (ethread % TPR) * 4;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  // 1. A rank that does not own the slice publishes it (the staging half is
-  //    free: group_unit_start checked it): rows scratch -> staging, scratch
-  //    re-zeroed, flag on the owner. The owner reads its own rows straight
-  //    from its scratch in step 2.
-  float* stage = g.stage[g.rank];
+  // 1. A rank that does not own the slice pushes it into its slot of the
+  //    owner's staging half (free: group_unit_start checked it): rows
+  //    scratch -> owner, scratch re-zeroed, flag on the owner. The owner
+  //    reads its own rows straight from its scratch in step 2.
   if (owner != g.rank) {
+    float* stage = g.stage[owner] + g.rank * g.slot_floats;
     for (int rr0 = r_begin + tr; rr0 < r_end; rr0 += 4 * RPI) {
       float4 v[4];
 #pragma unroll
@@ -215,14 +218,16 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
         __stcg(reinterpret_cast<float4*>(stage + off), v[b]);
       }
     }
+    fence_acq_rel_sys();    // this thread's peer stores, before the barrier
     named_barrier(1, 128);  // orders every thread's stores before the release
     if (ethread == 0) st_release_sys_u64(g.ready[owner] + static_cast<size_t>(slice) * g.world + g.rank, tag);
     return;
   }
   // 2. Owner: one thread per other rank polls that rank's flag; then every
-  //    rank's rows (peer loads, this rank's own from its scratch; all loads
-  //    of a row batch in flight at once), summed in rank order, bias, fp16
-  //    into the root's C; this rank's scratch rows re-zeroed.
+  //    rank's rows (its slot of this rank's staging, this rank's own from its
+  //    scratch; all loads of a row batch in flight at once), summed in rank
+  //    order, bias, fp16 into the root's C; this rank's scratch rows
+  //    re-zeroed.
   const bool ok = ethread >= g.world || ethread == g.rank ||
                   wait_all_ge_sys_u64(g.ready[g.rank] + static_cast<size_t>(slice) * g.world + ethread, 1, tag, wd,
                                       SITE_GEMM_GROUP_FLAGS);
@@ -246,7 +251,7 @@ __device__ __forceinline__ void group_finalize(const GemmArgs& args, int ctr_til
       for (int b = 0; b < RB; ++b) {
         const int rr = rr0 + b * RPI;
         if (src < g.world && rr < r_end) {
-          const float* from = src == g.rank ? args.ws : g.stage[src];
+          const float* from = src == g.rank ? args.ws : g.stage[g.rank] + src * g.slot_floats;
           v[src][b] = __ldcg(reinterpret_cast<const float4*>(from + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
         }
       }

@@ -20,7 +20,8 @@ static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(mm4_peer_handle), "IPC handle
 struct mm4_splitk_group {
   int world, rank, root, owner_mode;
   int num_slices;
-  size_t half_bytes;  // one staging half
+  size_t half_bytes;  // one staging half (world slots)
+  size_t slot_bytes;  // one rank's slot of a half
   unsigned long long epoch;
   char* exchange[MM4_MAX_GROUP];
   unsigned long long* ready[MM4_MAX_GROUP];
@@ -36,11 +37,13 @@ struct mm4_splitk_group {
 
 namespace {
 
-// Exchange buffer of one rank: staging half 0 | half 1 (each [stage_rows]
-// [ws_ld] fp32, 256-aligned) | ready [num_slices][world] u64 |
-// consumed [num_slices] u64 | done [num_slices] u64 (used on the root).
+// Exchange buffer of one rank: staging half 0 | half 1 (each [world slots]
+// [stage_rows][ws_ld] fp32, slots and halves 256-aligned) | ready
+// [num_slices][world] u64 | consumed [num_slices] u64 | done [num_slices] u64
+// (used on the root). Rank r pushes the slices an owner finishes into slot r
+// of the owner's half.
 struct ExchangeLayout {
-  size_t half_bytes, ready_offset, consumed_offset, done_offset, total;
+  size_t slot_bytes, half_bytes, ready_offset, consumed_offset, done_offset, total;
 };
 
 ExchangeLayout exchange_layout(const mm4_gemm_plan* p, int world) {
@@ -49,7 +52,8 @@ ExchangeLayout exchange_layout(const mm4_gemm_plan* p, int world) {
   const size_t num_slices = static_cast<size_t>(p->num_tiles) * halves * p->splits;
   const size_t stage_rows = static_cast<size_t>(p->num_m_tiles) * (p->pair ? 256 : 128);
   const size_t ws_ld = static_cast<size_t>(p->num_n_tiles) * p->bn;
-  L.half_bytes = (stage_rows * ws_ld * sizeof(float) + 255) & ~static_cast<size_t>(255);
+  L.slot_bytes = (stage_rows * ws_ld * sizeof(float) + 255) & ~static_cast<size_t>(255);
+  L.half_bytes = L.slot_bytes * static_cast<size_t>(world);
   L.ready_offset = 2 * L.half_bytes;
   L.consumed_offset = L.ready_offset + num_slices * world * sizeof(unsigned long long);
   L.done_offset = L.consumed_offset + num_slices * sizeof(unsigned long long);
@@ -66,12 +70,13 @@ mm4_status check_group_plan(const mm4_gemm_plan* p, int world) {
   return MM4_OK;
 }
 
-// Which ranks finish the slices. The root alone (default): one hop, the root
-// reads (world-1) partials over NVLink. Spread (MM4_SPLITK_GROUP_OWNERS=
-// spread): rank slice % world finishes the slice, reading (world-1)/world of
-// the partials, then writes the root's C and raises a done flag there, a
-// second hop. Measured on B200 (512x512, K 65536 per rank, split 32): root
-// 56.5 / 63.7 us per step at 2 / 4 ranks, spread 67.2 / 73.9 us.
+// Which ranks finish the slices. The root alone (default): one hop, the
+// other ranks push (world-1) partials into the root over NVLink. Spread
+// (MM4_SPLITK_GROUP_OWNERS=spread): rank slice % world finishes the slice,
+// receiving (world-1)/world of the partials, then writes the root's C and
+// raises a done flag there, a second hop. Measured on B200 with the earlier
+// pull design (512x512, K 65536 per rank, split 32): root 56.5 / 63.7 us per
+// step at 2 / 4 ranks, spread 67.2 / 73.9 us.
 int choose_owner_mode(int /*world*/) {
   const char* v = std::getenv("MM4_SPLITK_GROUP_OWNERS");
   if (v && std::strcmp(v, "spread") == 0) return 1;
@@ -164,6 +169,7 @@ mm4_status mm4_splitk_group_create(mm4_splitk_group** out, const mm4_gemm_plan* 
   g->halves = plan->pair ? 2 : 1;
   g->num_slices = plan->num_tiles * g->halves * plan->splits;
   g->half_bytes = L.half_bytes;
+  g->slot_bytes = L.slot_bytes;
   g->epoch = 0;
   for (int r = 0; r < world; ++r) {
     char* base = static_cast<char*>(exchange[r]);
@@ -209,6 +215,7 @@ mm4_status mm4_gemm_splitk_group_run(const mm4_gemm_plan* plan, mm4_splitk_group
   ga.owner_mode = g->owner_mode;
   ga.num_slices = g->num_slices;
   ga.epoch = g->epoch;
+  ga.slot_floats = static_cast<long long>(g->slot_bytes / sizeof(float));
   const size_t half = static_cast<size_t>(g->epoch & 1ull) * g->half_bytes;
   for (int r = 0; r < g->world; ++r) {
     ga.stage[r] = reinterpret_cast<float*>(g->exchange[r] + half);

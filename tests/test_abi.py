@@ -170,11 +170,12 @@ def test_splitk_group_sizing_and_validation():
     rc, plan = _gemm(M=512, N=512, K=65536, split_k=32)
     assert rc == 0
     nbytes = ctypes.c_size_t()
-    # staging: 2 halves x [512 rows][512] fp32; flags: ready 128 slices x world, consumed + done 128 each
+    # staging: 2 halves x world slots x [512 rows][512] fp32 (each rank pushes into its slot of the
+    # owner's half); flags: ready 128 slices x world, consumed + done 128 each
     for world in (1, 2, 8):
         assert lib.mm4_splitk_group_exchange_bytes(plan, world, ctypes.byref(nbytes)) == 0
         slices = 2 * 2 * 32  # 2 pair tiles x 2 row halves x 32 splits
-        assert nbytes.value == 2 * 512 * 512 * 4 + slices * world * 8 + 2 * slices * 8
+        assert nbytes.value == 2 * world * 512 * 512 * 4 + slices * world * 8 + 2 * slices * 8
     assert lib.mm4_splitk_group_exchange_bytes(plan, 9, ctypes.byref(nbytes)) == _lib.MM4_ERR_UNSUPPORTED
     assert lib.mm4_splitk_group_exchange_bytes(plan, 0, ctypes.byref(nbytes)) == _lib.MM4_ERR_UNSUPPORTED
     g = ctypes.c_void_p()
