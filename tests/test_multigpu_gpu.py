@@ -201,3 +201,35 @@ def test_two_ranks_nccl_bootstrapped_comm():
                 p.kill()
     assert kind == "ok", payload
     assert max(payload) <= 0.0, payload
+
+
+@pytest.mark.parametrize("owners", ["root", "spread"])
+def test_every_gpu_fused_splitk(owners):
+    """The fused split-K group on every GPU of the box (at least three, at most eight): ranks 2 and up
+    push into slots beyond the first two of the owner's staging, and with spread owners every rank owns
+    slices."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    n = torch.cuda.device_count()
+    if n < 3:
+        pytest.skip("needs three or more GPUs")
+    world = min(n, 8)
+    store = dist.TCPStore("127.0.0.1", 0, world_size=world + 1, is_master=True,
+                          timeout=datetime.timedelta(seconds=60), wait_for_workers=False)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, store.port, q, 512, 512, 8192, 32, 3, owners))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        kind, payload = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert kind == "ok", payload
+    assert max(payload) <= 0.0, payload
