@@ -94,6 +94,10 @@ struct GemmArgs {
   unsigned long long* counters;  // one arrival count per 128-row half tile, split-K only
   int ws_ld;
   int coop_finalize;      // split-K: all units co-resident (cooperative launch), slices finalized in parallel
+  // Split-K, deterministic mode (0: off): split s stores its partial into
+  // ws + s * det_split_floats instead of reducing it into ws, and the
+  // finalize sums the splits in order, so every run gives the same bits.
+  long long det_split_floats;
   // Output row map of the direct epilogue. 0: tile row r is output row
   // mt*128 + r (GEMM). 1: a tile is a rm_th x rm_tw rectangle of output
   // pixels of one (n, oz) plane (convolution with TMA-fed activations).
@@ -478,10 +482,18 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
         const int sub_r = lane >> 3;
         const int sub_c = (lane & 7) * 4;
         float* dst = args.ws + static_cast<size_t>(row_base + q * 32 + sub_r) * args.ws_ld + cbase + sub_c;
+        if (args.det_split_floats != 0) {
+          dst += w.split * args.det_split_floats;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float4 v = *reinterpret_cast<const float4*>(wst + (k * 4 + sub_r) * EPI_STAGE_LD + sub_c);
-          red_add_v4_f32(dst + static_cast<size_t>(k * 4) * args.ws_ld, v.x, v.y, v.z, v.w);
+          for (int k = 0; k < 8; ++k)
+            __stcg(reinterpret_cast<float4*>(dst + static_cast<size_t>(k * 4) * args.ws_ld),
+                   *reinterpret_cast<const float4*>(wst + (k * 4 + sub_r) * EPI_STAGE_LD + sub_c));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 v = *reinterpret_cast<const float4*>(wst + (k * 4 + sub_r) * EPI_STAGE_LD + sub_c);
+            red_add_v4_f32(dst + static_cast<size_t>(k * 4) * args.ws_ld, v.x, v.y, v.z, v.w);
+          }
         }
         __syncwarp();
       } else if constexpr (OUT_F32) {
@@ -606,16 +618,31 @@ __device__ __forceinline__ void epilogue_role(const GemmArgs& args, uint64_t* tm
 #pragma unroll
           for (int bb = 0; bb < 4; ++bb) {
             const int rr = rr0 + bb * RPI;
-            if (rr < r_end)
-              s4v[bb] = __ldcg(reinterpret_cast<const float4*>(args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc));
+            if (rr >= r_end) continue;
+            const float* src = args.ws + static_cast<size_t>(row_base + rr) * args.ws_ld + gc;
+            if (args.det_split_floats != 0) {
+              // The splits' partials, summed in split order.
+              float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
+              for (int sp = 1; sp < args.splits; ++sp) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + sp * args.det_split_floats));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+              }
+              s4v[bb] = acc;
+            } else {
+              s4v[bb] = __ldcg(reinterpret_cast<const float4*>(src));
+            }
           }
 #pragma unroll
           for (int bb = 0; bb < 4; ++bb) {
           const int rr = rr0 + bb * RPI;
           if (rr >= r_end) break;
           const int grow = row_base + rr;
-          __stcg(reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc),
-                 make_float4(0.f, 0.f, 0.f, 0.f));
+          if (args.det_split_floats == 0)
+            __stcg(reinterpret_cast<float4*>(args.ws + static_cast<size_t>(grow) * args.ws_ld + gc),
+                   make_float4(0.f, 0.f, 0.f, 0.f));
           if (grow >= args.M) continue;
           const float4 s4 = s4v[bb];
           const float o0 = s4.x + b0, o1 = s4.y + b1, o2 = s4.z + b2, o3 = s4.w + b3;

@@ -59,6 +59,15 @@ mm4_status run_simt(const mm4_gemm_plan* p, const void* A, const void* B, const 
 // MM4_SPLITK_COOPERATIVE=0 selects the last-arriver finalize even where every
 // work unit fits on the device at once (profilers that replay kernels may not
 // support cooperative launches of clusters).
+// MM4_SPLITK_DETERMINISTIC=1, read when a plan is created: split-K partials
+// are stored one slice per split and summed in split order (bitwise
+// reproducible runs; splits x the partial bytes of workspace, and more
+// traffic than the default in-L2 reduction). Single-GPU plans only.
+bool deterministic_splitk_requested() {
+  const char* v = std::getenv("MM4_SPLITK_DETERMINISTIC");
+  return v && v[0] == '1';
+}
+
 bool cooperative_finalize_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("MM4_SPLITK_COOPERATIVE");
@@ -102,6 +111,7 @@ mm4_status gemm_run_tc(const mm4_gemm_plan* p, const void* A, const void* B, con
     if (!aligned16(ws)) return fail(MM4_ERR_WORKSPACE, "workspace must be 16-byte aligned");
     args.ws = static_cast<float*>(ws);
     args.counters = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + p->ws_counter_offset);
+    args.det_split_floats = p->det_split_floats;
     // The cooperative finalize has every split of a tile meet in the
     // epilogue, so it needs all CTAs co-resident and no two splits of one
     // tile on the same CTA (pair): one CTA (pair) per (split, M-tile).
@@ -114,6 +124,8 @@ mm4_status gemm_run_tc(const mm4_gemm_plan* p, const void* A, const void* B, con
     mode = out_f32 ? MODE_DIRECT_F32 : MODE_DIRECT_F16;
   }
   if (grp && grp->world > 1) {
+    if (p->det_split_floats != 0)
+      return fail(MM4_ERR_UNSUPPORTED, "the deterministic split-K mode is single-GPU only");
     if (p->splits < 2 || out_f32)
       return fail(MM4_ERR_UNSUPPORTED, "a multi-GPU split-K group needs a split-K plan (split_k >= 2)");
     if (!args.coop_finalize)
@@ -200,9 +212,15 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   p->num_tiles = p->num_m_tiles * p->num_n_tiles;
   p->ws_bytes = 0;
   p->ws_counter_offset = 0;
+  p->det_split_floats = 0;
   if (p->splits > 1) {
     const int tile_m = p->pair ? 2 * GEMM_BM : GEMM_BM;
-    const size_t acc = static_cast<size_t>(p->num_m_tiles) * tile_m * p->num_n_tiles * p->bn * sizeof(float);
+    size_t acc = static_cast<size_t>(p->num_m_tiles) * tile_m * p->num_n_tiles * p->bn * sizeof(float);
+    if (deterministic_splitk_requested() && p->tensor_core) {
+      // One partial slice per split, summed in split order by the finalize.
+      p->det_split_floats = static_cast<long long>(acc / sizeof(float));
+      acc *= static_cast<size_t>(p->splits);
+    }
     p->ws_counter_offset = acc;
     // one 64-bit arrival counter per 128-row half tile
     const size_t counters = static_cast<size_t>(p->num_tiles) * (p->pair ? 2 : 1) * sizeof(unsigned long long);
@@ -211,7 +229,8 @@ mm4_status mm4_gemm_plan_create(mm4_gemm_plan** out, const mm4_gemm_desc* desc) 
   if (p->tensor_core)
     snprintf(p->name, sizeof(p->name), "gemm_sm100%s<BM=%d,BN=%d,%s%s,%s>", p->pair ? "_pair" : "",
              p->pair ? 2 * GEMM_BM : GEMM_BM, p->bn, d.transpose_left ? "A:MN" : "A:K",
-             d.transpose_right ? ",B:K" : ",B:MN", p->splits > 1 ? "splitk" : "direct");
+             d.transpose_right ? ",B:K" : ",B:MN",
+             p->splits > 1 ? (p->det_split_floats != 0 ? "splitk-deterministic" : "splitk") : "direct");
   else
     snprintf(p->name, sizeof(p->name), "gemm_simt<unaligned>");
   *out = p;

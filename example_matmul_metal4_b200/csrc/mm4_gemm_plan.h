@@ -17,6 +17,7 @@ struct mm4_gemm_plan {
   int num_m_tiles, num_n_tiles, num_tiles;
   size_t ws_bytes;
   size_t ws_counter_offset;
+  long long det_split_floats;  // split-K deterministic mode: floats per split's partial (0: off)
   char name[96];
 };
 

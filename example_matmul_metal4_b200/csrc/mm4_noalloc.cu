@@ -178,6 +178,7 @@ mm4_status mm4_gemm_splitk_run_noalloc(const mm4_gemm_plan* p, const void* A, co
   args.C32 = nullptr;
   args.ws = static_cast<float*>(scratch);
   args.counters = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + p->ws_counter_offset);
+  args.det_split_floats = p->det_split_floats;
   args.coop_finalize = 0;  // the last-arriving unit of each tile finalizes it
   args.status = status;
   args.timeout_ns = wait_timeout_ns();

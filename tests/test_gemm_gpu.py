@@ -160,3 +160,30 @@ def test_bounded_wait_reports_timeout_and_context_survives(cuda):
 def test_invalid_descriptor_rejected():
     with pytest.raises(MM4Error):
         GemmPlan(GEMMDimensions(0, 16, 16))
+
+
+@pytest.mark.parametrize("M,N,K,split,tr", [(512, 512, 65536, 32, False), (32, 3072, 80000, 30, True),
+                                            (640, 768, 4160, 7, False)])
+def test_deterministic_split_k(cuda, monkeypatch, M, N, K, split, tr):
+    """MM4_SPLITK_DETERMINISTIC=1 (read when the plan is created): each split stores its partial and the
+    finalize sums the splits in order, so repeated runs give identical bits; within tolerance of the oracle
+    (rows at both ends; all rows for the smaller shapes). Covers the cooperative finalize (512x512, the
+    BASELINE shape), the last-arriver finalize (the reference's 32x3072x80000 NT run) and a K tail."""
+    import torch
+    monkeypatch.setenv("MM4_SPLITK_DETERMINISTIC", "1")
+    A, B, b = _inputs(M, N, K, False, tr, 9)
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, tr), bias=True, buildOptions=BuildOptions(splitK=split))
+    assert "splitk-deterministic" in plan.kernel_name
+    tA, tB, tb = (torch.from_numpy(x).to(cuda) for x in (A, B, b))
+    ws = plan.workspace(cuda)
+    first = plan.run(tA, tB, tb, workspace=ws).clone()
+    for _ in range(3):
+        again = plan.run(tA, tB, tb, workspace=ws)
+        sync_check()
+        assert torch.equal(again, first)
+    rows = (0, M) if M * N <= 640 * 768 else (0, 8)
+    ref = oracle.gemm(A, B, b, M, N, K, False, tr, rows=rows, threads=oracle.default_threads())
+    assert_close(first.float().cpu().numpy()[rows[0]:rows[1]], ref, f"deterministic split {split}")
+    if M * N > 640 * 768:
+        ref2 = oracle.gemm(A, B, b, M, N, K, False, tr, rows=(M - 8, M), threads=oracle.default_threads())
+        assert_close(first.float().cpu().numpy()[M - 8:M], ref2, f"deterministic split {split} last rows")
