@@ -179,35 +179,6 @@ mm4_status launch_backward(const CUtensorMap& tq, const CUtensorMap& tk, const C
   return MM4_OK;
 }
 
-// Side streams and events of the host-buffer forward, created once per device.
-constexpr int kHostMaxChunks = 64;
-struct HostPipe {
-  bool ready = false;
-  cudaStream_t in = nullptr, out = nullptr;
-  cudaEvent_t start, end, loaded[kHostMaxChunks], done[kHostMaxChunks];
-};
-constexpr int kHostMaxDevices = 64;
-HostPipe g_host_pipe[kHostMaxDevices];
-std::mutex g_host_mutex;
-
-mm4_status host_pipe(int dev, HostPipe** out) {
-  if (dev < 0 || dev >= kHostMaxDevices) return fail(MM4_ERR_CUDA, "device id %d out of range", dev);
-  HostPipe& hp = g_host_pipe[dev];
-  if (!hp.ready) {
-    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.in, cudaStreamNonBlocking));
-    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.out, cudaStreamNonBlocking));
-    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.start, cudaEventDisableTiming));
-    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.end, cudaEventDisableTiming));
-    for (int i = 0; i < kHostMaxChunks; ++i) {
-      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.loaded[i], cudaEventDisableTiming));
-      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.done[i], cudaEventDisableTiming));
-    }
-    hp.ready = true;
-  }
-  *out = &hp;
-  return MM4_OK;
-}
-
 int padded_rows(const mm4_attention_desc& d) { return (d.rows + ATT_BM - 1) / ATT_BM * ATT_BM; }
 
 size_t bwd_workspace_bytes(const mm4_attention_desc& d) {
@@ -247,7 +218,7 @@ mm4_status mm4_attention_fwd_host(const mm4_attention_plan* p, const void* hQ, c
   n = static_cast<int>(std::min<long long>(std::min(n, kHostMaxChunks), pieces));
   int dev = -1;
   MM4_CUDA_TRY(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(g_host_mutex);
+  std::lock_guard<std::mutex> lock(host_pipe_mutex());
   HostPipe* hp = nullptr;
   mm4_status rc = host_pipe(dev, &hp);
   if (rc != MM4_OK) return rc;
@@ -366,7 +337,7 @@ mm4_status mm4_attention_bwd_host(const mm4_attention_plan* p, const void* const
   n = static_cast<int>(std::min<long long>(std::min(n, kHostMaxChunks), pieces));
   int dev = -1;
   MM4_CUDA_TRY(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(g_host_mutex);
+  std::lock_guard<std::mutex> lock(host_pipe_mutex());
   HostPipe* hp = nullptr;
   mm4_status rc = host_pipe(dev, &hp);
   if (rc != MM4_OK) return rc;

@@ -266,6 +266,86 @@ mm4_status mm4_gemm_run(const mm4_gemm_plan* p, const void* A, const void* B, co
   return MM4_OK;
 }
 
+mm4_status mm4_gemm_run_host(const mm4_gemm_plan* p, const void* hA, const void* hB, const void* hbias, void* hC,
+                             void* dA, void* dB, void* dbias, void* dC, void* workspace, size_t workspace_bytes,
+                             int32_t chunks, mm4_stream_t stream) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!hA || !hB || !hC || !dA || !dB || !dC) return fail(MM4_ERR_INVALID, "null buffer pointer");
+  if (p->d.bias && (!hbias || !dbias)) return fail(MM4_ERR_INVALID, "plan has bias but a bias pointer is null");
+  const mm4_gemm_desc& d = p->d;
+  const size_t a_row = static_cast<size_t>(d.K) * 2, c_row = static_cast<size_t>(d.N) * 2;
+  // Chunks of whole 256-row blocks of A and C; A must be [M][K] for its rows
+  // to be contiguous (otherwise one chunk).
+  int n = chunks > 0 ? chunks : 16;
+  const int blocks = (d.M + 255) / 256;
+  if (d.transpose_left) n = 1;
+  n = std::max(1, std::min(std::min(n, kHostMaxChunks), blocks));
+  const int rows_per = (blocks + n - 1) / n * 256;
+  n = (d.M + rows_per - 1) / rows_per;
+  // Plans of the chunk heights (all but the last share one).
+  mm4_gemm_plan* sub[2] = {nullptr, nullptr};
+  auto cleanup = [&]() {
+    for (auto*& q : sub)
+      if (q) {
+        mm4_gemm_plan_destroy(q);
+        q = nullptr;
+      }
+  };
+  const int last_rows = d.M - (n - 1) * rows_per;
+  for (int i = 0; i < 2; ++i) {
+    mm4_gemm_desc sd = d;
+    sd.M = i == 0 ? std::min(rows_per, d.M) : last_rows;
+    mm4_status rc = mm4_gemm_plan_create(&sub[i], &sd);
+    if (rc != MM4_OK) {
+      cleanup();
+      return rc;
+    }
+  }
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cleanup();
+    return cuda_fail(e, "cudaGetDevice");
+  }
+  std::lock_guard<std::mutex> lock(host_pipe_mutex());
+  HostPipe* hp = nullptr;
+  mm4_status rc = host_pipe(dev, &hp);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+  auto run = [&]() -> mm4_status {
+    if (rc != MM4_OK) return rc;
+    MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+    // B and bias first: every chunk needs them whole.
+    const size_t b_bytes = static_cast<size_t>(d.K) * d.N * 2;
+    MM4_CUDA_TRY(cudaMemcpyAsync(dB, hB, b_bytes, cudaMemcpyHostToDevice, hp->in));
+    if (d.bias) MM4_CUDA_TRY(cudaMemcpyAsync(dbias, hbias, c_row, cudaMemcpyHostToDevice, hp->in));
+    for (int c = 0; c < n; ++c) {
+      const int m0 = c * rows_per, rows = c == n - 1 ? last_rows : rows_per;
+      const size_t ao = d.transpose_left ? 0 : static_cast<size_t>(m0) * a_row;
+      const size_t an = d.transpose_left ? static_cast<size_t>(d.K) * d.M * 2 : static_cast<size_t>(rows) * a_row;
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dA, ao), at(hA, ao), an, cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+      const size_t co = static_cast<size_t>(m0) * c_row;
+      mm4_status r = mm4_gemm_run(c == n - 1 ? sub[1] : sub[0], at(dA, ao), dB, d.bias ? dbias : nullptr,
+                                  at(dC, co), workspace, workspace_bytes, stream, 1);
+      if (r != MM4_OK) return r;
+      MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(hC, co), at(dC, co), static_cast<size_t>(rows) * c_row,
+                                   cudaMemcpyDeviceToHost, hp->out));
+    }
+    MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+    return MM4_OK;
+  };
+  rc = run();
+  cleanup();
+  return rc;
+}
+
 mm4_status mm4_gemm_partial_run(const mm4_gemm_plan* p, const void* A, const void* B, float* C32, void* workspace,
                                 size_t workspace_bytes, mm4_stream_t stream) {
   if (!p) return fail(MM4_ERR_INVALID, "null plan");

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "mm4.h"
@@ -22,6 +23,20 @@ mm4_status cuda_fail(cudaError_t err, const char* what);
     cudaError_t mm4_e_ = (expr);                            \
     if (mm4_e_ != cudaSuccess) return ::mm4::cuda_fail(mm4_e_, #expr); \
   } while (0)
+
+// Two library streams and a pool of events per device for the host-buffer
+// entry points (copies in on `in`, copies out on `out`, the kernels on the
+// caller's stream), created on first use and kept for the process.
+constexpr int kHostMaxChunks = 64;
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start, end, loaded[kHostMaxChunks], done[kHostMaxChunks];
+};
+// The pipe of device `dev`; call with host_pipe_mutex() held for the whole
+// enqueue of one call.
+mm4_status host_pipe(int dev, HostPipe** out);
+std::mutex& host_pipe_mutex();
 
 // Current device id, its SM count and whether it is an sm_100 part.
 struct DeviceInfo {

@@ -94,6 +94,32 @@ mm4_status status_word(int** ptr) {
 
 uint64_t wait_timeout_ns() { return g_timeout_ns.load(); }
 
+namespace {
+constexpr int kHostMaxDevices = 64;
+HostPipe g_host_pipe[kHostMaxDevices];
+std::mutex g_host_mutex;
+}  // namespace
+
+std::mutex& host_pipe_mutex() { return g_host_mutex; }
+
+mm4_status host_pipe(int dev, HostPipe** out) {
+  if (dev < 0 || dev >= kHostMaxDevices) return fail(MM4_ERR_CUDA, "device id %d out of range", dev);
+  HostPipe& hp = g_host_pipe[dev];
+  if (!hp.ready) {
+    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.in, cudaStreamNonBlocking));
+    MM4_CUDA_TRY(cudaStreamCreateWithFlags(&hp.out, cudaStreamNonBlocking));
+    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.start, cudaEventDisableTiming));
+    MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.end, cudaEventDisableTiming));
+    for (int i = 0; i < kHostMaxChunks; ++i) {
+      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.loaded[i], cudaEventDisableTiming));
+      MM4_CUDA_TRY(cudaEventCreateWithFlags(&hp.done[i], cudaEventDisableTiming));
+    }
+    hp.ready = true;
+  }
+  *out = &hp;
+  return MM4_OK;
+}
+
 mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                         CUtensorMapSwizzle swizzle) {

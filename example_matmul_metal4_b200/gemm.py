@@ -103,6 +103,30 @@ class GemmPlan:
                                         int(duplicatedCount)))
         return C
 
+    def run_host(self, A, B, bias, C, staging, workspace=None, chunks: int = 16, stream=None):
+        """C = A*B (+bias) for CPU tensors (pinned for the copies to overlap) through the CUDA tensors
+        staging = (dA, dB, dbias, dC) of the full shapes (dbias may be None without bias): B and bias are
+        copied in first, then A's row blocks, their GEMMs and C's row blocks run as a pipeline over
+        `chunks` pieces (mm4_gemm_run_host). Ordered on `stream`."""
+        import torch
+        d = self.dims
+        dA, dB, db, dC = staging
+        _check_tensor(dA, self.a_shape(), "dA")
+        _check_tensor(dB, self.b_shape(), "dB")
+        _check_tensor(dC, (d.M, d.N), "dC")
+        if self.bias:
+            _check_tensor(db, (d.N,), "dbias")
+        for name, h, shape in (("A", A, self.a_shape()), ("B", B, self.b_shape()), ("C", C, (d.M, d.N))):
+            if h.is_cuda or h.dtype != torch.float16 or not h.is_contiguous() or tuple(h.shape) != tuple(shape):
+                raise ValueError(f"{name} must be a contiguous CPU fp16 tensor of shape {tuple(shape)}")
+        ws = workspace if workspace is not None else self.workspace(dA.device)
+        _lib.check(self._L.mm4_gemm_run_host(
+            self._h, A.data_ptr(), B.data_ptr(), bias.data_ptr() if self.bias else None, C.data_ptr(),
+            dA.data_ptr(), dB.data_ptr(), db.data_ptr() if self.bias else None, dC.data_ptr(),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, int(chunks),
+            _lib.stream_handle(stream)))
+        return C
+
     def partial(self, A, B, C32=None, workspace=None, stream=None):
         """fp32 partial A*B over this plan's K (no bias), for cross-rank split-K."""
         import torch

@@ -116,6 +116,19 @@ typedef struct mm4_gemm_plan mm4_gemm_plan;
 MM4_API mm4_status mm4_gemm_plan_create(mm4_gemm_plan** plan, const mm4_gemm_desc* desc);
 MM4_API void mm4_gemm_plan_destroy(mm4_gemm_plan* plan);
 
+/* C = A * B (+ bias) from and to host memory (page-locked for the copies to
+ * overlap), through the caller's device buffers dA, dB, dbias, dC of the
+ * plan's full sizes and the plan's workspace. B and bias are copied in
+ * first; then, for `chunks` blocks of 256-row multiples of A and C (<= 0: 16;
+ * one when A is stored [K][M]), the copy of A's rows, the GEMM on them and the
+ * copy of C's rows out run as a pipeline on `stream` and two library streams.
+ * Each block runs as a GEMM of its own height, so a split-K plan's blocks may
+ * differ from one whole-problem run in the last fp32 bit; direct plans give
+ * mm4_gemm_run's bits. */
+MM4_API mm4_status mm4_gemm_run_host(const mm4_gemm_plan* plan, const void* hA, const void* hB, const void* hbias,
+                                     void* hC, void* dA, void* dB, void* dbias, void* dC, void* workspace,
+                                     size_t workspace_bytes, int32_t chunks, mm4_stream_t stream);
+
 /* Bytes of device workspace mm4_gemm_run needs (0 when split_k <= 1). The
  * workspace must be zero-filled before its first use (mm4_workspace_clear);
  * every run leaves it zero-filled again. Runs sharing a workspace must not

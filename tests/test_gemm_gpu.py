@@ -187,3 +187,32 @@ def test_deterministic_split_k(cuda, monkeypatch, M, N, K, split, tr):
     if M * N > 640 * 768:
         ref2 = oracle.gemm(A, B, b, M, N, K, False, tr, rows=(M - 8, M), threads=oracle.default_threads())
         assert_close(first.float().cpu().numpy()[M - 8:M], ref2, f"deterministic split {split} last rows")
+
+
+@pytest.mark.parametrize("M,N,K,tl,tr,split", [(1000, 768, 1024, False, False, 1), (1024, 1024, 1024, False, True, 1),
+                                               (512, 640, 4096, True, False, 1), (768, 512, 8192, False, False, 8)])
+def test_host_buffer_gemm(cuda, M, N, K, tl, tr, split):
+    """mm4_gemm_run_host (pinned host A, B, bias in, C out, pipelined over 256-row blocks): the bits of
+    mm4_gemm_run for direct plans (row blocks, a ragged last block, B stored [N][K], A stored [K][M] as one
+    block), and within tolerance of the oracle for a split-K plan, whose blocks are GEMMs of their own."""
+    import torch
+    A, B, b = _inputs(M, N, K, tl, tr, 11)
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(tl, tr), bias=True, buildOptions=BuildOptions(splitK=split))
+    tA, tB, tb = (torch.from_numpy(x).to(cuda) for x in (A, B, b))
+    ref = plan.run(tA, tB, tb).cpu()
+    sync_check()
+    hA, hB, hb = (x.cpu().pin_memory() for x in (tA, tB, tb))
+    hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    staging = (torch.empty_like(tA), torch.empty_like(tB), torch.empty_like(tb),
+               torch.empty((M, N), dtype=torch.float16, device=cuda))
+    for chunks in (1, 3, 64):
+        hC.fill_(float("nan"))
+        plan.run_host(hA, hB, hb, hC, staging, chunks=chunks)
+        sync_check()
+        if split == 1:
+            assert torch.equal(hC, ref), chunks
+        else:
+            got = hC.float().numpy()
+            assert_close(got[:8], oracle.gemm(A, B, b, M, N, K, tl, tr, rows=(0, 8), threads=oracle.default_threads()),
+                         f"host-buffer split-K chunks={chunks}")
+            assert_close(got, ref.float().numpy(), f"host-buffer split-K vs device run, chunks={chunks}")
