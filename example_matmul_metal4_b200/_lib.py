@@ -108,6 +108,7 @@ SIGNATURES = {
     "mm4_attention_plan_kernel_name": (ctypes.c_char_p, [_vp]),
     "mm4_attention_fwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int]),
     "mm4_attention_fwd_lse": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "mm4_conv_run_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp]),
     "mm4_gemm_run_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, ctypes.c_int32, _vp]),
     "mm4_attention_fwd_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp]),
     "mm4_attention_bwd_host": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, ctypes.c_int32, _vp]),

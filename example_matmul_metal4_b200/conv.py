@@ -184,6 +184,32 @@ class ConvPlan:
                                         _lib.stream_handle(stream), int(duplicatedCount)))
         return y
 
+    def run_host(self, x, w, bias, y, staging, chunks: int = 16, stream=None):
+        """y = conv(x, w) (+bias) for CPU tensors (pinned for the copies to overlap) through the CUDA tensors
+        staging = (dx, dw, dbias, dy) of the full shapes (dbias may be None without bias): the weights and
+        bias are copied in first, then groups of batch elements are copied in, convolved and copied out as a
+        pipeline over `chunks` pieces (mm4_conv_run_host). Ordered on `stream`."""
+        import torch
+        dx, dw, db, dy = staging
+        for name, t, shape, cuda in (("x", x, self.in_shape, False), ("y", y, self.out_shape, False),
+                                     ("dx", dx, self.in_shape, True), ("dy", dy, self.out_shape, True)):
+            if t.is_cuda != cuda or t.dtype != torch.float16 or not t.is_contiguous() or tuple(t.shape) != shape:
+                where = "CUDA" if cuda else "CPU"
+                raise ValueError(f"{name} must be a contiguous {where} fp16 tensor of shape {shape}")
+        for name, t, cuda in (("w", w, False), ("dw", dw, True)):
+            if t.numel() != self.weight_elements or t.dtype != torch.float16 or t.is_cuda != cuda \
+                    or not t.is_contiguous():
+                raise ValueError(f"{name} must hold the plan's weights as contiguous fp16")
+        if self.bias:
+            for name, t, cuda in (("bias", bias, False), ("dbias", db, True)):
+                if t is None or t.numel() != self.dims.outputChannels or t.is_cuda != cuda:
+                    raise ValueError(f"{name} of Cout elements is required")
+        _lib.check(self._L.mm4_conv_run_host(
+            self._h, x.data_ptr(), w.data_ptr(), bias.data_ptr() if self.bias else None, y.data_ptr(),
+            dx.data_ptr(), dw.data_ptr(), db.data_ptr() if self.bias else None, dy.data_ptr(), int(chunks),
+            _lib.stream_handle(stream)))
+        return y
+
 
 def permute_weights(src, from_layout: int, to_layout: int, dims5, stream=None, dst=None):
     """Weight layout transform on the GPU; dims5 = (Cout, Cin, KD, KH, KW). Writes `dst` (same size as

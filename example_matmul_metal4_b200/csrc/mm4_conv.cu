@@ -33,6 +33,9 @@ struct mm4_conv_plan {
   long long m_virtual;  // taprow: N * OD * OH * vw tile rows
   int tw, th;        // output rectangle per tile on the rectangle path (tw * th = 128)
   int tiles_w, tiles_h;
+  int dims;            // 2 or 3: the descriptor the plan was created from
+  mm4_conv2d_desc d2;  // (for plans of a batch chunk, mm4_conv_run_host)
+  mm4_conv3d_desc d3;
   char name[96];
 };
 
@@ -199,6 +202,8 @@ mm4_status mm4_conv2d_plan_create(mm4_conv_plan** out, const mm4_conv2d_desc* d)
   g.OW = out_size(g.W, d->padding_left, d->padding_right, g.KW, g.SX, g.DX);
   g.w_layout = d->weight_layout;
   p->bias = d->bias ? 1 : 0;
+  p->dims = 2;
+  p->d2 = *d;
   rc = finish_plan(p);
   if (rc != MM4_OK) {
     delete p;
@@ -246,6 +251,8 @@ mm4_status mm4_conv3d_plan_create(mm4_conv_plan** out, const mm4_conv3d_desc* d)
   g.OW = out_size(g.W, d->padding_left, d->padding_right, g.KW, g.SX, g.DX);
   g.w_layout = d->weight_layout;
   p->bias = d->bias ? 1 : 0;
+  p->dims = 3;
+  p->d3 = *d;
   rc = finish_plan(p);
   if (rc != MM4_OK) {
     delete p;
@@ -273,6 +280,87 @@ mm4_status mm4_conv_plan_tile_grid(const mm4_conv_plan* p, int32_t grid[3]) {
 
 int64_t mm4_conv_output_elements(const mm4_conv_plan* plan) {
   return plan ? plan->m_total * plan->g.O : 0;
+}
+
+mm4_status mm4_conv_run_host(const mm4_conv_plan* p, const void* hx, const void* hw, const void* hbias, void* hy,
+                             void* dx, void* dw, void* dbias, void* dy, int32_t chunks, mm4_stream_t stream) {
+  if (!p) return fail(MM4_ERR_INVALID, "null plan");
+  if (!hx || !hw || !hy || !dx || !dw || !dy) return fail(MM4_ERR_INVALID, "null buffer pointer");
+  if (p->bias && (!hbias || !dbias)) return fail(MM4_ERR_INVALID, "plan has bias but a bias pointer is null");
+  const ConvGeom& g = p->g;
+  const size_t x_img = static_cast<size_t>(g.D) * g.H * g.W * g.C * 2;
+  const size_t y_img = static_cast<size_t>(g.OD) * g.OH * g.OW * g.O * 2;
+  const size_t w_bytes = static_cast<size_t>(g.taps) * g.C * g.O * 2, b_bytes = static_cast<size_t>(g.O) * 2;
+  int n = chunks > 0 ? chunks : 16;
+  n = std::max(1, std::min(std::min(n, kHostMaxChunks), g.N));
+  const int per = (g.N + n - 1) / n;
+  n = (g.N + per - 1) / per;
+  const int last = g.N - (n - 1) * per;
+  // Plans of the chunk batch sizes (all but the last share one).
+  mm4_conv_plan* sub[2] = {nullptr, nullptr};
+  auto cleanup = [&]() {
+    for (auto*& q : sub)
+      if (q) {
+        mm4_conv_plan_destroy(q);
+        q = nullptr;
+      }
+  };
+  for (int i = 0; i < 2; ++i) {
+    const int nb = i == 0 ? std::min(per, g.N) : last;
+    mm4_status rc;
+    if (p->dims == 2) {
+      mm4_conv2d_desc d = p->d2;
+      d.batch_size = nb;
+      rc = mm4_conv2d_plan_create(&sub[i], &d);
+    } else {
+      mm4_conv3d_desc d = p->d3;
+      d.batch_size = nb;
+      rc = mm4_conv3d_plan_create(&sub[i], &d);
+    }
+    if (rc != MM4_OK) {
+      cleanup();
+      return rc;
+    }
+  }
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cleanup();
+    return cuda_fail(e, "cudaGetDevice");
+  }
+  std::lock_guard<std::mutex> lock(host_pipe_mutex());
+  HostPipe* hp = nullptr;
+  mm4_status rc = host_pipe(dev, &hp);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+  auto run = [&]() -> mm4_status {
+    if (rc != MM4_OK) return rc;
+    MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+    // Weights and bias first: every chunk needs them whole.
+    MM4_CUDA_TRY(cudaMemcpyAsync(dw, hw, w_bytes, cudaMemcpyHostToDevice, hp->in));
+    if (p->bias) MM4_CUDA_TRY(cudaMemcpyAsync(dbias, hbias, b_bytes, cudaMemcpyHostToDevice, hp->in));
+    for (int c = 0; c < n; ++c) {
+      const int nb = c == n - 1 ? last : per;
+      const size_t xo = static_cast<size_t>(c) * per * x_img, yo = static_cast<size_t>(c) * per * y_img;
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dx, xo), at(hx, xo), nb * x_img, cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+      mm4_status r = mm4_conv_run(c == n - 1 ? sub[1] : sub[0], at(dx, xo), dw, p->bias ? dbias : nullptr,
+                                  at(dy, yo), stream, 1);
+      if (r != MM4_OK) return r;
+      MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(hy, yo), at(dy, yo), nb * y_img, cudaMemcpyDeviceToHost, hp->out));
+    }
+    MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+    return MM4_OK;
+  };
+  rc = run();
+  cleanup();
+  return rc;
 }
 
 mm4_status mm4_conv_run(const mm4_conv_plan* p, const void* x, const void* w, const void* bias, void* y,

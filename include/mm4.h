@@ -387,6 +387,15 @@ MM4_API const char* mm4_conv_plan_kernel_name(const mm4_conv_plan* plan);
 MM4_API mm4_status mm4_conv_plan_tile_grid(const mm4_conv_plan* plan, int32_t grid[3]);
 /* Output element count of the plan (N*OD*OH*OW*Cout). */
 MM4_API int64_t mm4_conv_output_elements(const mm4_conv_plan* plan);
+/* y = conv(x, w) (+ bias) from and to host memory (page-locked for the
+ * copies to overlap), through the caller's device buffers of the plan's
+ * full sizes: the weights and bias are copied in first, then `chunks` groups
+ * of whole batch elements (<= 0: 16) are copied in, convolved and copied out
+ * as a pipeline on `stream` and two library streams. Each output pixel is
+ * computed as in mm4_conv_run. */
+MM4_API mm4_status mm4_conv_run_host(const mm4_conv_plan* plan, const void* hx, const void* hw, const void* hbias,
+                                     void* hy, void* dx, void* dw, void* dbias, void* dy, int32_t chunks,
+                                     mm4_stream_t stream);
 /* y = conv(x, w) (+ bias). */
 MM4_API mm4_status mm4_conv_run(const mm4_conv_plan* plan, const void* x, const void* w, const void* bias, void* y,
                         mm4_stream_t stream, int duplicated_count);

@@ -284,3 +284,30 @@ def test_permute_weights_exact(cuda, src, dst, kd):
     sync_check()
     ref = oracle.permute_weights(w, src, dst, O, C, kd, KH, KW)
     assert np.array_equal(got.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("three_d,chunks", [(False, 3), (True, 2), (False, 64)])
+def test_host_buffer_conv_matches_device_conv(cuda, three_d, chunks):
+    """mm4_conv_run_host (images copied in, convolved and copied out in batch chunks, ragged last chunk)
+    writes the same bits as mm4_conv_run on device buffers."""
+    import torch
+    if three_d:
+        d = Conv3DDimensions(5, 4, 12, 12, 64, 64, 3, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1)
+        plan = ConvPlan(d, weight_layout=WEIGHTS_ODHWI, bias=True)
+        w_shape = (64, 3, 3, 3, 64)
+    else:
+        d = Conv2DDimensions(7, 20, 20, 64, 128, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1)
+        plan = ConvPlan(d, weight_layout=WEIGHTS_OHWI, bias=True)
+        w_shape = (128, 3, 3, 64)
+    x = torch.from_numpy(data.normal(plan.in_shape, 1.0, 6, 0)).pin_memory()
+    w = torch.from_numpy(data.normal(w_shape, 0.05, 6, 1)).pin_memory()
+    b = torch.from_numpy(data.uniform((d.outputChannels,), -0.1, 0.1, 6, 2)).pin_memory()
+    y = torch.empty(plan.out_shape, dtype=torch.float16).pin_memory()
+    staging = (torch.empty_like(x, device=cuda), torch.empty_like(w, device=cuda), torch.empty_like(b, device=cuda),
+               torch.empty(plan.out_shape, dtype=torch.float16, device=cuda))
+    plan.run_host(x, w, b, y, staging, chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    sync_check()
+    ref = plan.run(x.to(cuda), w.to(cuda), b.to(cuda))
+    sync_check()
+    assert torch.equal(y, ref.cpu())
