@@ -252,3 +252,60 @@ def test_header_is_plain_c_and_the_library_links_from_c(tmp_path):
     lines = r.stdout.splitlines()
     assert lines[0].startswith("gemm_sm100_pair<") and "splitk" in lines[0]
     assert lines[1].endswith("2112 1 1") and "taprow" in lines[1]
+
+
+def test_host_buffer_entry_points_validate_before_any_copy():
+    """The host-buffer pipelines (mm4_gemm_run_host, mm4_conv_run_host, mm4_attention_fwd_host,
+    mm4_attention_bwd_host) reject a null plan, a null buffer and a missing bias or workspace before any
+    copy or launch is queued, so these calls need no device."""
+    lib = _lib.lib()
+    fake = 1 << 20  # stand-in pointers: every call below fails before a pointer is dereferenced
+    INVALID, WORKSPACE = _lib.MM4_ERR_INVALID, _lib.MM4_ERR_WORKSPACE
+
+    rc, g = _gemm(M=512, N=256, K=1024, bias=1)
+    assert rc == 0
+    args = [fake] * 8  # hA hB hbias hC dA dB dbias dC
+    assert lib.mm4_gemm_run_host(None, *args, None, 0, 4, None) == INVALID
+    for i in range(8):
+        bad = list(args)
+        bad[i] = None
+        assert lib.mm4_gemm_run_host(g, *bad, None, 0, 4, None) == INVALID
+    assert b"null" in lib.mm4_last_error()
+    lib.mm4_gemm_plan_destroy(g)
+
+    h = ctypes.c_void_p()
+    d2 = _lib.Conv2dDesc(3, 9, 9, 16, 32, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, _lib.WEIGHTS_OHWI, 1)
+    assert lib.mm4_conv2d_plan_create(ctypes.byref(h), ctypes.byref(d2)) == 0
+    args = [fake] * 8  # hx hw hbias hy dx dw dbias dy
+    assert lib.mm4_conv_run_host(None, *args, 2, None) == INVALID
+    for i in range(8):
+        bad = list(args)
+        bad[i] = None
+        assert lib.mm4_conv_run_host(h, *bad, 2, None) == INVALID
+    assert b"bias" in lib.mm4_last_error() or b"null" in lib.mm4_last_error()
+    lib.mm4_conv_plan_destroy(h)
+
+    a = _lib.AttentionDesc(2, 8, 2, 200, 333, 128, 0.0, _lib.MM4_ATTN_BSHD)
+    assert lib.mm4_attention_plan_create(ctypes.byref(h), ctypes.byref(a)) == 0
+    args = [fake] * 8  # hQ hK hV hO dQ dK dV dO
+    assert lib.mm4_attention_fwd_host(None, *args, 4, None) == INVALID
+    for i in range(8):
+        bad = list(args)
+        bad[i] = None
+        assert lib.mm4_attention_fwd_host(h, *bad, 4, None) == INVALID
+
+    def arr(n, hole=None):
+        return (ctypes.c_void_p * n)(*[None if i == hole else fake for i in range(n)])
+    ws = lib.mm4_attention_bwd_workspace_size(h)
+    assert lib.mm4_attention_bwd_host(None, arr(6), arr(3), arr(6), arr(3), fake, ws, 4, None) == INVALID
+    assert lib.mm4_attention_bwd_host(h, None, arr(3), arr(6), arr(3), fake, ws, 4, None) == INVALID
+    for i in range(6):
+        assert lib.mm4_attention_bwd_host(h, arr(6, i), arr(3), arr(6), arr(3), fake, ws, 4, None) == INVALID
+        assert lib.mm4_attention_bwd_host(h, arr(6), arr(3), arr(6, i), arr(3), fake, ws, 4, None) == INVALID
+    for i in range(3):
+        assert lib.mm4_attention_bwd_host(h, arr(6), arr(3, i), arr(6), arr(3), fake, ws, 4, None) == INVALID
+        assert lib.mm4_attention_bwd_host(h, arr(6), arr(3), arr(6), arr(3, i), fake, ws, 4, None) == INVALID
+    assert lib.mm4_attention_bwd_host(h, arr(6), arr(3), arr(6), arr(3), None, ws, 4, None) == WORKSPACE
+    assert lib.mm4_attention_bwd_host(h, arr(6), arr(3), arr(6), arr(3), fake, ws - 16, 4, None) == WORKSPACE
+    assert b"workspace" in lib.mm4_last_error()
+    lib.mm4_attention_plan_destroy(h)
