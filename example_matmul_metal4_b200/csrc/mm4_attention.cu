@@ -223,38 +223,43 @@ mm4_status mm4_attention_fwd_host(const mm4_attention_plan* p, const void* hQ, c
   mm4_status rc = host_pipe(dev, &hp);
   if (rc != MM4_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
-  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
-  for (int c = 0; c < n; ++c) {
-    const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
-    const size_t qo = static_cast<size_t>(p0) * q_piece, qn = static_cast<size_t>(np) * q_piece;
-    const size_t ko = static_cast<size_t>(p0) * kv_piece, kn = static_cast<size_t>(np) * kv_piece;
-    MM4_CUDA_TRY(cudaMemcpyAsync(at(dQ, qo), at(hQ, qo), qn, cudaMemcpyHostToDevice, hp->in));
-    MM4_CUDA_TRY(cudaMemcpyAsync(at(dK, ko), at(hK, ko), kn, cudaMemcpyHostToDevice, hp->in));
-    MM4_CUDA_TRY(cudaMemcpyAsync(at(dV, ko), at(hV, ko), kn, cudaMemcpyHostToDevice, hp->in));
-    MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
-    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
-    // The chunk as a problem of its own: its (batch, head) units are
-    // computed exactly as in the whole problem.
-    mm4_attention_plan sub = *p;
-    if (bhsd) {
-      sub.d.batch = 1;
-      sub.d.heads_q = static_cast<int32_t>(np * group);
-      sub.d.heads_kv = static_cast<int32_t>(np);
-    } else {
-      sub.d.batch = static_cast<int32_t>(np);
+  auto run = [&]() -> mm4_status {
+    MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+    auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+    for (int c = 0; c < n; ++c) {
+      const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
+      const size_t qo = static_cast<size_t>(p0) * q_piece, qn = static_cast<size_t>(np) * q_piece;
+      const size_t ko = static_cast<size_t>(p0) * kv_piece, kn = static_cast<size_t>(np) * kv_piece;
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dQ, qo), at(hQ, qo), qn, cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dK, ko), at(hK, ko), kn, cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(dV, ko), at(hV, ko), kn, cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+      // The chunk as a problem of its own: its (batch, head) units are
+      // computed exactly as in the whole problem.
+      mm4_attention_plan sub = *p;
+      if (bhsd) {
+        sub.d.batch = 1;
+        sub.d.heads_q = static_cast<int32_t>(np * group);
+        sub.d.heads_kv = static_cast<int32_t>(np);
+      } else {
+        sub.d.batch = static_cast<int32_t>(np);
+      }
+      mm4_status r = attention_forward(&sub, at(dQ, qo), at(dK, ko), at(dV, ko), at(dO, qo), nullptr, st, 1);
+      if (r != MM4_OK) return r;
+      MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+      MM4_CUDA_TRY(cudaMemcpyAsync(at(hO, qo), at(dO, qo), qn, cudaMemcpyDeviceToHost, hp->out));
     }
-    rc = attention_forward(&sub, at(dQ, qo), at(dK, ko), at(dV, ko), at(dO, qo), nullptr, st, 1);
-    if (rc != MM4_OK) return rc;
-    MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
-    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
-    MM4_CUDA_TRY(cudaMemcpyAsync(at(hO, qo), at(dO, qo), qn, cudaMemcpyDeviceToHost, hp->out));
-  }
-  MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
-  return MM4_OK;
+    MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+    return MM4_OK;
+  };
+  rc = run();
+  if (rc != MM4_OK) host_pipe_join(hp, st);
+  return rc;
 }
 
 size_t mm4_attention_bwd_workspace_size(const mm4_attention_plan* p) { return p ? bwd_workspace_bytes(p->d) : 0; }
@@ -342,43 +347,49 @@ mm4_status mm4_attention_bwd_host(const mm4_attention_plan* p, const void* const
   mm4_status rc = host_pipe(dev, &hp);
   if (rc != MM4_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
-  auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
-  for (int c = 0; c < n; ++c) {
-    const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
-    // Offsets and sizes of the chunk in Q / O / dO (and dQ), K / V (and dK, dV), lse.
-    const size_t qo = p0 * q_piece, qn = np * q_piece, ko = p0 * kv_piece, kn = np * kv_piece;
-    const size_t lo = p0 * l_piece, ln = np * l_piece;
-    const size_t in_off[6] = {qo, ko, ko, qo, qo, lo}, in_len[6] = {qn, kn, kn, qn, qn, ln};
-    for (int i = 0; i < 6; ++i)
-      MM4_CUDA_TRY(cudaMemcpyAsync(at(dev_in[i], in_off[i]), at(host_in[i], in_off[i]), in_len[i],
-                                   cudaMemcpyHostToDevice, hp->in));
-    MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
-    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
-    mm4_attention_plan sub = *p;
-    if (bhsd) {
-      sub.d.batch = 1;
-      sub.d.heads_q = static_cast<int32_t>(np * group);
-      sub.d.heads_kv = static_cast<int32_t>(np);
-    } else {
-      sub.d.batch = static_cast<int32_t>(np);
+  auto run = [&]() -> mm4_status {
+    MM4_CUDA_TRY(cudaEventRecord(hp->start, st));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->in, hp->start, 0));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->start, 0));
+    auto at = [](const void* base, size_t off) { return static_cast<char*>(const_cast<void*>(base)) + off; };
+    for (int c = 0; c < n; ++c) {
+      const long long p0 = c * pieces / n, p1 = (c + 1) * pieces / n, np = p1 - p0;
+      // Offsets and sizes of the chunk in Q / O / dO (and dQ), K / V (and dK, dV), lse.
+      const size_t qo = p0 * q_piece, qn = np * q_piece, ko = p0 * kv_piece, kn = np * kv_piece;
+      const size_t lo = p0 * l_piece, ln = np * l_piece;
+      const size_t in_off[6] = {qo, ko, ko, qo, qo, lo}, in_len[6] = {qn, kn, kn, qn, qn, ln};
+      for (int i = 0; i < 6; ++i)
+        MM4_CUDA_TRY(cudaMemcpyAsync(at(dev_in[i], in_off[i]), at(host_in[i], in_off[i]), in_len[i],
+                                     cudaMemcpyHostToDevice, hp->in));
+      MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
+      mm4_attention_plan sub = *p;
+      if (bhsd) {
+        sub.d.batch = 1;
+        sub.d.heads_q = static_cast<int32_t>(np * group);
+        sub.d.heads_kv = static_cast<int32_t>(np);
+      } else {
+        sub.d.batch = static_cast<int32_t>(np);
+      }
+      mm4_status r = mm4_attention_bwd(
+          &sub, at(dev_in[0], qo), at(dev_in[1], ko), at(dev_in[2], ko), at(dev_in[3], qo), at(dev_in[4], qo),
+          reinterpret_cast<const float*>(at(dev_in[5], lo)), at(dev_out[0], qo), at(dev_out[1], ko),
+          at(dev_out[2], ko), at(workspace, p0 * w_piece), np * w_piece, stream);
+      if (r != MM4_OK) return r;
+      MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
+      MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
+      const size_t out_off[3] = {qo, ko, ko}, out_len[3] = {qn, kn, kn};
+      for (int i = 0; i < 3; ++i)
+        MM4_CUDA_TRY(cudaMemcpyAsync(at(host_out[i], out_off[i]), at(dev_out[i], out_off[i]), out_len[i],
+                                     cudaMemcpyDeviceToHost, hp->out));
     }
-    rc = mm4_attention_bwd(&sub, at(dev_in[0], qo), at(dev_in[1], ko), at(dev_in[2], ko), at(dev_in[3], qo),
-                           at(dev_in[4], qo), reinterpret_cast<const float*>(at(dev_in[5], lo)), at(dev_out[0], qo),
-                           at(dev_out[1], ko), at(dev_out[2], ko), at(workspace, p0 * w_piece), np * w_piece, stream);
-    if (rc != MM4_OK) return rc;
-    MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
-    MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));
-    const size_t out_off[3] = {qo, ko, ko}, out_len[3] = {qn, kn, kn};
-    for (int i = 0; i < 3; ++i)
-      MM4_CUDA_TRY(cudaMemcpyAsync(at(host_out[i], out_off[i]), at(dev_out[i], out_off[i]), out_len[i],
-                                   cudaMemcpyDeviceToHost, hp->out));
-  }
-  MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
-  MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
-  return MM4_OK;
+    MM4_CUDA_TRY(cudaEventRecord(hp->end, hp->out));
+    MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->end, 0));
+    return MM4_OK;
+  };
+  rc = run();
+  if (rc != MM4_OK) host_pipe_join(hp, st);
+  return rc;
 }
 
 }  // extern "C"

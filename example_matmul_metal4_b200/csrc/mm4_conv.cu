@@ -359,6 +359,7 @@ mm4_status mm4_conv_run_host(const mm4_conv_plan* p, const void* hx, const void*
     return MM4_OK;
   };
   rc = run();
+  if (rc != MM4_OK) host_pipe_join(hp, st);
   cleanup();
   return rc;
 }

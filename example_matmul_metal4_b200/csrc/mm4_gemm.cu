@@ -342,6 +342,7 @@ mm4_status mm4_gemm_run_host(const mm4_gemm_plan* p, const void* hA, const void*
     return MM4_OK;
   };
   rc = run();
+  if (rc != MM4_OK) host_pipe_join(hp, st);
   cleanup();
   return rc;
 }

@@ -37,6 +37,10 @@ struct HostPipe {
 // enqueue of one call.
 mm4_status host_pipe(int dev, HostPipe** out);
 std::mutex& host_pipe_mutex();
+// After an error part-way through an enqueue: orders `st` after whatever was
+// already queued on the pipe's streams (best effort), so that synchronising
+// `st` still means no copy of the call touches the caller's buffers any more.
+void host_pipe_join(HostPipe* hp, cudaStream_t st);
 
 // Current device id, its SM count and whether it is an sm_100 part.
 struct DeviceInfo {

@@ -120,6 +120,12 @@ mm4_status host_pipe(int dev, HostPipe** out) {
   return MM4_OK;
 }
 
+void host_pipe_join(HostPipe* hp, cudaStream_t st) {
+  if (!hp || !hp->ready) return;
+  if (cudaEventRecord(hp->start, hp->in) == cudaSuccess) (void)cudaStreamWaitEvent(st, hp->start, 0);
+  if (cudaEventRecord(hp->end, hp->out) == cudaSuccess) (void)cudaStreamWaitEvent(st, hp->end, 0);
+}
+
 mm4_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* base,
                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                         CUtensorMapSwizzle swizzle) {

@@ -124,7 +124,7 @@ MM4_API void mm4_gemm_plan_destroy(mm4_gemm_plan* plan);
  * copy of C's rows out run as a pipeline on `stream` and two library streams.
  * Each block runs as a GEMM of its own height, so a split-K plan's blocks may
  * differ from one whole-problem run in the last fp32 bit; direct plans give
- * mm4_gemm_run's bits. */
+ * mm4_gemm_run's bits. Ordering and errors as for mm4_attention_fwd_host. */
 MM4_API mm4_status mm4_gemm_run_host(const mm4_gemm_plan* plan, const void* hA, const void* hB, const void* hbias,
                                      void* hC, void* dA, void* dB, void* dbias, void* dC, void* workspace,
                                      size_t workspace_bytes, int32_t chunks, mm4_stream_t stream);
@@ -291,7 +291,8 @@ MM4_API mm4_status mm4_attention_fwd_lse(const mm4_attention_plan* plan, const v
  * call for callers whose tensors live on the host. Ordered on `stream`:
  * work queued on it before the call precedes the copies, and later work
  * follows the last copy out. Results equal mm4_attention_fwd's bit for
- * bit. */
+ * bit. A call that fails part-way still orders `stream` after every copy it
+ * queued, so synchronising `stream` before freeing the buffers stays safe. */
 MM4_API mm4_status mm4_attention_fwd_host(const mm4_attention_plan* plan, const void* hQ, const void* hK,
                                           const void* hV, void* hO, void* dQ, void* dK, void* dV, void* dO,
                                           int32_t chunks, mm4_stream_t stream);
@@ -392,7 +393,8 @@ MM4_API int64_t mm4_conv_output_elements(const mm4_conv_plan* plan);
  * full sizes: the weights and bias are copied in first, then `chunks` groups
  * of whole batch elements (<= 0: 16) are copied in, convolved and copied out
  * as a pipeline on `stream` and two library streams. Each output pixel is
- * computed as in mm4_conv_run. */
+ * computed as in mm4_conv_run. Ordering and errors as for
+ * mm4_attention_fwd_host. */
 MM4_API mm4_status mm4_conv_run_host(const mm4_conv_plan* plan, const void* hx, const void* hw, const void* hbias,
                                      void* hy, void* dx, void* dw, void* dbias, void* dy, int32_t chunks,
                                      mm4_stream_t stream);
