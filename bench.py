@@ -776,6 +776,14 @@ def run_mm4(args, w, dist, peaks):
 # CPU legs (oracle = the reference's CPU loops restated in C)
 # ---------------------------------------------------------------------------
 
+def whole_rounds(rows, threads, total):
+    """A row count for a sample on `threads` threads: a whole number of rows per thread, so that no thread
+    idles at the end and the rate does not depend on how the last round splits (at most `total`)."""
+    if total <= threads:
+        return total
+    return min(total // threads * threads, max(threads, rows // threads * threads))
+
+
 def cpu_sample(w, seconds_hint=10.0, threads=None):
     """Times the oracle on a bounded sample of workload `w`, extrapolated to the full workload."""
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -799,8 +807,9 @@ def cpu_sample(w, seconds_hint=10.0, threads=None):
     if isinstance(w, GemmWorkload):
         M, N, K = w.M, w.N, w.K
         A, B, bias = h((M, K), uniform=True), h((K, N), uniform=True), h((N,), uniform=True)
-        one = timed(lambda: oracle.gemm(A, B, bias, M, N, K, rows=(0, 1), threads=1))
-        rows = max(1, min(M, int(seconds_hint * threads / max(one, 1e-6))))
+        # An untimed round of one row per thread warms the pages and threads and sizes the sample.
+        one = timed(lambda: oracle.gemm(A, B, bias, M, N, K, rows=(0, min(M, threads)), threads=threads))
+        rows = whole_rounds(int(seconds_hint / max(one, 1e-6)) * threads, threads, M)
         dt = timed(lambda: oracle.gemm(A, B, bias, M, N, K, rows=(0, rows), threads=threads))
         flops = 2.0 * rows * N * K
         sample = (f"{rows} of {M} output rows of the {M}x{N}x{K} GEMM+bias (fp32 loop of matmul.swift:499-510), "
@@ -843,8 +852,8 @@ def cpu_sample(w, seconds_hint=10.0, threads=None):
             kw = dict(N=1, H=w.H, W=w.W, C=w.C, O=w.O, KH=3, KW=3, pad_top=1, pad_bottom=1, pad_left=1,
                       pad_right=1, layout=1)
             total_rows, per_row_flops, fn = w.H, 2.0 * w.W * w.O * 9 * w.C, oracle.conv2d
-        one = timed(lambda: fn(x, wt, b, rows=(0, 1), threads=1, **kw))
-        rows = max(1, min(total_rows, int(seconds_hint * threads / max(one, 1e-6))))
+        one = timed(lambda: fn(x, wt, b, rows=(0, min(total_rows, threads)), threads=threads, **kw))
+        rows = whole_rounds(int(seconds_hint / max(one, 1e-6)) * threads, threads, total_rows)
         dt = timed(lambda: fn(x, wt, b, rows=(0, rows), threads=threads, **kw))
         flops = per_row_flops * rows
         sample = (f"{rows} output rows ({w.W} pixels x {w.O} channels each) of one image of the {w.name} conv "

@@ -82,3 +82,15 @@ def test_strong_scaling_shards_cover_each_named_shape_once():
             units += nb * nh
         assert units == att.B * att.H
     assert att.shard(2, 1) == (2, 16) and att.shard(8, 3) == (1, 8)
+
+
+def test_cpu_sample_rows_are_whole_rounds_per_thread():
+    """The CPU baseline's row samples give every thread the same number of rows (no idle thread in the
+    last round), and never exceed the workload."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.whole_rounds(198, 16, 512) == 192
+    assert bench.whole_rounds(5, 16, 512) == 16
+    assert bench.whole_rounds(10**6, 16, 512) == 512
+    assert bench.whole_rounds(100, 16, 56) == 48
+    assert bench.whole_rounds(100, 16, 10) == 10
