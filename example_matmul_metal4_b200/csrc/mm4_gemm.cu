@@ -296,11 +296,26 @@ mm4_status mm4_gemm_run_host(const mm4_gemm_plan* p, const void* hA, const void*
     mm4_gemm_desc sd = d;
     sd.M = i == 0 ? std::min(rows_per, d.M) : last_rows;
     mm4_status rc = mm4_gemm_plan_create(&sub[i], &sd);
+    if (rc == MM4_OK && (sub[i]->det_split_floats != 0) != (p->det_split_floats != 0))
+      rc = fail(MM4_ERR_INVALID, "MM4_SPLITK_DETERMINISTIC changed since the plan was created");
     if (rc != MM4_OK) {
       cleanup();
       return rc;
     }
   }
+  // The block plans run on the whole plan's workspace, shifted so that their
+  // split-K arrival counters are the whole plan's counters and their partials
+  // lie inside its partial area. Counters then stay multiples of the split
+  // count whichever plan ran last, and the partial area keeps its invariant
+  // (zero-filled, or overwritten whole in the deterministic mode).
+  auto block_ws = [&](const mm4_gemm_plan* q, void** w, size_t* bytes) {
+    *w = workspace;
+    *bytes = workspace_bytes;
+    if (!workspace || q->ws_bytes == 0 || p->ws_bytes == 0 || q->ws_counter_offset >= p->ws_counter_offset) return;
+    const size_t delta = p->ws_counter_offset - q->ws_counter_offset;
+    *w = static_cast<char*>(workspace) + delta;
+    *bytes = workspace_bytes > delta ? workspace_bytes - delta : 0;
+  };
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -329,8 +344,11 @@ mm4_status mm4_gemm_run_host(const mm4_gemm_plan* p, const void* hA, const void*
       MM4_CUDA_TRY(cudaEventRecord(hp->loaded[c], hp->in));
       MM4_CUDA_TRY(cudaStreamWaitEvent(st, hp->loaded[c], 0));
       const size_t co = static_cast<size_t>(m0) * c_row;
-      mm4_status r = mm4_gemm_run(c == n - 1 ? sub[1] : sub[0], at(dA, ao), dB, d.bias ? dbias : nullptr,
-                                  at(dC, co), workspace, workspace_bytes, stream, 1);
+      const mm4_gemm_plan* q = c == n - 1 ? sub[1] : sub[0];
+      void* qws = nullptr;
+      size_t qws_bytes = 0;
+      block_ws(q, &qws, &qws_bytes);
+      mm4_status r = mm4_gemm_run(q, at(dA, ao), dB, d.bias ? dbias : nullptr, at(dC, co), qws, qws_bytes, stream, 1);
       if (r != MM4_OK) return r;
       MM4_CUDA_TRY(cudaEventRecord(hp->done[c], st));
       MM4_CUDA_TRY(cudaStreamWaitEvent(hp->out, hp->done[c], 0));

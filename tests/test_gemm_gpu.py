@@ -216,3 +216,44 @@ def test_host_buffer_gemm(cuda, M, N, K, tl, tr, split):
             assert_close(got[:8], oracle.gemm(A, B, b, M, N, K, tl, tr, rows=(0, 8), threads=oracle.default_threads()),
                          f"host-buffer split-K chunks={chunks}")
             assert_close(got, ref.float().numpy(), f"host-buffer split-K vs device run, chunks={chunks}")
+
+
+@pytest.mark.parametrize("deterministic", [False, True])
+def test_host_buffer_and_device_runs_share_one_workspace(cuda, monkeypatch, deterministic):
+    """A split-K plan's workspace serves mm4_gemm_run and mm4_gemm_run_host in any order: the host-buffer
+    path's block plans use the plan's own arrival counters, so neither path leaves the other a counter that
+    is not a multiple of the split count or a partial area that is not clean. Deterministic mode gives the
+    same bits on every repeat of each path."""
+    import torch
+    if deterministic:
+        monkeypatch.setenv("MM4_SPLITK_DETERMINISTIC", "1")
+    else:
+        monkeypatch.delenv("MM4_SPLITK_DETERMINISTIC", raising=False)
+    M, N, K, split = 768, 768, 8192, 8
+    A, B, b = _inputs(M, N, K, False, False, 13)
+    plan = GemmPlan(GEMMDimensions(M, N, K), transpose=(False, False), bias=True,
+                    buildOptions=BuildOptions(splitK=split))
+    assert ("splitk-deterministic" in plan.kernel_name) == deterministic
+    tA, tB, tb = (torch.from_numpy(x).to(cuda) for x in (A, B, b))
+    ws = plan.workspace(cuda)
+    hA, hB, hb = (x.cpu().pin_memory() for x in (tA, tB, tb))
+    staging = (torch.empty_like(tA), torch.empty_like(tB), torch.empty_like(tb),
+               torch.empty((M, N), dtype=torch.float16, device=cuda))
+    dev_runs, host_runs = [], []
+    for _ in range(3):
+        dev_runs.append(plan.run(tA, tB, tb, workspace=ws).cpu())
+        sync_check()
+        hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
+        plan.run_host(hA, hB, hb, hC, staging, workspace=ws, chunks=3)
+        sync_check()
+        host_runs.append(hC.clone())
+    ref = oracle.gemm(A, B, b, M, N, K, rows=(0, 8), threads=oracle.default_threads())
+    ref_end = oracle.gemm(A, B, b, M, N, K, rows=(M - 8, M), threads=oracle.default_threads())
+    for i, (c, h) in enumerate(zip(dev_runs, host_runs)):
+        for name, got in (("device", c), ("host-buffer", h)):
+            g = got.float().numpy()
+            assert_close(g[:8], ref, f"{name} run {i}, first rows")
+            assert_close(g[M - 8:], ref_end, f"{name} run {i}, last rows")
+        assert_close(h.float().numpy(), dev_runs[0].float().numpy(), f"host-buffer run {i} vs device run")
+        if deterministic:
+            assert torch.equal(c, dev_runs[0]) and torch.equal(h, host_runs[0]), i
